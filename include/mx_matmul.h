@@ -1,0 +1,179 @@
+/*
+ * mx_matmul.h -- C ABI of the B200-native dense-matmul path for moonxi-net.
+ *
+ * This library replaces the reference's Linear/MLP matmul path behind its own
+ * C stub layer.  Reference paths below are relative to the moonxi-net project
+ * root.  Every entry point takes plain pointers and sizes, returns an int32
+ * status (0 = success, see MX_* codes) and never aborts the process.
+ *
+ * Pointers are raw device pointers owned by the caller (the reference's bump
+ * pool hands out 256-byte aligned blocks, moonxi-net-gpu/cuda/cuda_kernels.cu
+ * :922-1004; any 4-byte aligned pointer is accepted).  All launches are
+ * asynchronous on the context's stream (the legacy default stream unless set),
+ * exactly like the reference's cuBLAS call.
+ *
+ * `handle`: the reference passes an opaque handle (its cuBLAS handle from
+ * gpu_init, moonxi-net-gpu/cuda/gpu_context.mbt:67-71).  A handle created by
+ * mx_context_create() selects that context; any other value (NULL, or a
+ * cuBLAS handle the caller still passes) selects the default context of the
+ * current device.  Unknown handles are never dereferenced.
+ */
+#ifndef MX_MATMUL_H
+#define MX_MATMUL_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MX_OK 0
+#define MX_ERR_INVALID 1     /* bad argument (negative size, null pointer, ...) */
+#define MX_ERR_UNSUPPORTED 2 /* shape/stride this build cannot run            */
+#define MX_ERR_CUDA 3        /* a CUDA runtime call failed                      */
+#define MX_ERR_TIMEOUT 4     /* a bounded in-kernel wait gave up                */
+#define MX_ERR_NOMEM 5       /* workspace allocation failed                     */
+#define MX_ERR_NO_DEVICE 6   /* no usable CUDA device                           */
+
+/* Precision modes for the contraction. */
+#define MX_PREC_DEFAULT 0 /* the context's mode (env MX_MATMUL_PRECISION, else AUTO) */
+#define MX_PREC_AUTO 1    /* fp32-class: 3xTF32 tensor cores for large shapes, FP32 SIMT otherwise */
+#define MX_PREC_FP32 2    /* exact-fp32 SIMT (FFMA) kernel                     */
+#define MX_PREC_3XTF32 3  /* tcgen05 3xTF32 split, fp32-class accuracy         */
+#define MX_PREC_TF32 4    /* tcgen05 plain TF32 (opt-in, ~1e-3 relative)       */
+
+/* ---------------------------------------------------------------------- */
+/* Reference-compatible entry points                                       */
+/* ---------------------------------------------------------------------- */
+
+/* Replaces `cuda_matmul` (moonxi-net-gpu/cuda/cuda_kernels.cu:1464-1499).
+ * Row-major C[M,N] = alpha * op(A) op(B) + beta * C.
+ * transpose_a = 0: A stored [M,K]; 1: A stored [K,M] and used transposed.
+ * transpose_b = 0: B stored [K,N]; 1: B stored [N,K] and used transposed.
+ * beta == 0 never reads C.  Uses the context's precision mode. */
+int cuda_matmul(void* handle, float* a, float* b, float* c, int M, int K, int N,
+                int transpose_a, int transpose_b, float alpha, float beta);
+
+/* Replaces `moonbit_cuda_matmul` (moonxi-net-gpu/cuda/cuda_stub.c:948-969),
+ * the stub bound by `extern "c" fn moonbit_cuda_matmul`
+ * (moonxi-net-gpu/cuda/ffi.mbt:526-539).  Same signature and semantics. */
+int32_t moonbit_cuda_matmul(void* handle, void* a, void* b, void* c, int32_t M, int32_t K,
+                            int32_t N, int32_t transpose_a, int32_t transpose_b, float alpha,
+                            float beta);
+
+/* ---------------------------------------------------------------------- */
+/* New entry points on the same path                                        */
+/* ---------------------------------------------------------------------- */
+
+/* moonbit_cuda_matmul with an explicit stream (NULL = context stream) and
+ * precision (MX_PREC_*).  Extends moonxi-net-gpu/cuda/cuda_stub.c:948-969. */
+int32_t moonbit_cuda_matmul_ex(void* handle, void* a, void* b, void* c, int32_t M, int32_t K,
+                               int32_t N, int32_t transpose_a, int32_t transpose_b, float alpha,
+                               float beta, void* stream, int32_t precision);
+
+/* Fused Linear forward: y[M,N] = act(alpha * x[M,K] op(w) + bias[N]), act =
+ * ReLU when relu != 0.  transpose_w = 0: w stored [K,N] (Linear::forward,
+ * moonxi-net/model/layers.mbt:59-64); 1: w stored [N,K] (MLP::forward,
+ * moonxi-net/model/mlp.mbt:16-23).  bias may be NULL.  Replaces the
+ * reference's matmul + add + relu sequence (tensor/trait_impl.mbt:209-250,
+ * cuda_kernels.cu:132-139 elementwise_add, :795-810 cuDNN ReLU) and its dead
+ * gpu_linear (moonxi-net-gpu/tensor/linear.mbt:5-37).  The bias is a true
+ * row broadcast, added after the matmul is rounded (NpArray order). */
+int32_t moonbit_cuda_linear_fwd(void* handle, void* x, void* w, void* bias, void* y, int32_t M,
+                                int32_t K, int32_t N, int32_t transpose_w, int32_t relu,
+                                float alpha);
+
+/* moonbit_cuda_linear_fwd with explicit stream and precision. */
+int32_t moonbit_cuda_linear_fwd_ex(void* handle, void* x, void* w, void* bias, void* y,
+                                   int32_t M, int32_t K, int32_t N, int32_t transpose_w,
+                                   int32_t relu, float alpha, void* stream, int32_t precision);
+
+/* General form behind all of the above: C[M,N] = act(alpha op(A) op(B) +
+ * beta C + bias[N]) for any transpose flags, explicit leading dimensions
+ * (lda/ldb/ldc in elements; 0 = the packed default of cuda_matmul), bias may
+ * be NULL.  Used by the backward GEMMs and by tests of every layout. */
+int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float* c, const float* bias,
+                   int32_t M, int32_t K, int32_t N, int32_t transpose_a, int32_t transpose_b,
+                   int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, int32_t relu,
+                   void* stream, int32_t precision);
+
+/* cudaSetDevice for the calling host thread (the reference hard-codes
+ * device 0 at every call site, moonxi-net-gpu/cuda/gpu_context.mbt:57-83). */
+int32_t moonbit_cuda_set_device(int32_t device);
+
+/* ---------------------------------------------------------------------- */
+/* Contexts (the `handle`)                                                   */
+/* ---------------------------------------------------------------------- */
+
+/* Creates a context on `device` (allocates its status word).  NULL on error.
+ * Replaces the role of gpu_init's handle (gpu_context.mbt:67-71). */
+void* mx_context_create(int32_t device);
+void mx_context_destroy(void* handle);
+int32_t mx_context_set_stream(void* handle, void* stream);
+int32_t mx_context_set_precision(void* handle, int32_t precision);
+/* Bound (nanoseconds) on every in-kernel wait; default 2 s. */
+int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns);
+/* Pre-sizes the context workspace (split operands, split-K partials) so that
+ * later calls allocate nothing; required before CUDA-graph capture. */
+int32_t mx_context_reserve_workspace(void* handle, uint64_t bytes);
+/* Workspace bytes a matmul of this shape and precision would need. */
+uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K, int32_t N,
+                                   int32_t transpose_a, int32_t transpose_b, int32_t precision);
+/* Synchronises the context's device, returns the device status word
+ * (MX_ERR_TIMEOUT if a bounded wait gave up since the last query) and clears
+ * it.  `where` (may be NULL) receives the in-kernel call site code. */
+int32_t mx_context_status(void* handle, int32_t* where);
+/* Precision the dispatcher would pick for this call (MX_PREC_FP32,
+ * MX_PREC_3XTF32 or MX_PREC_TF32). */
+int32_t mx_matmul_resolve_precision(void* handle, int32_t M, int32_t K, int32_t N,
+                                    int32_t precision);
+const char* mx_status_string(int32_t status);
+/* Number of kernels this library has launched in this process (all devices);
+ * lets callers count the native launches inside a timed region. */
+uint64_t mx_kernel_launch_count(void);
+
+/* ---------------------------------------------------------------------- */
+/* The rest of one Linear/MLP training step (adjacent ops on the tape)      */
+/* ---------------------------------------------------------------------- */
+
+/* grad_in[i] = saved[i] > 0 ? grad_out[i] : 0 over n elements.  `saved` may
+ * be the ReLU input or its output (x > 0 <=> relu(x) > 0).  Replaces
+ * cudnn_relu_backward (cuda_kernels.cu:812-831), NpArray semantics
+ * moonxi-net/nparray/image_impl.mbt:146-159. */
+int32_t mx_relu_backward(void* handle, const float* grad_out, const float* saved,
+                         float* grad_in, int64_t n, void* stream);
+
+/* out[j] = sum_i in[i * output_numel + j] for i < lead_stride (bias
+ * gradient).  Same arguments as cuda_reduce_sum_leading
+ * (cuda_kernels.cu:1383-1406); deterministic fixed-order tree sum. */
+int32_t mx_reduce_sum_leading(void* handle, const float* in, float* out, int32_t output_numel,
+                              int32_t lead_stride, void* stream);
+
+/* Softmax cross-entropy with integer labels (stored as floats), forward and
+ * backward in one pass: loss[0] = sum_rows(-log_softmax[label]) / denom and
+ * grad[b,j] = (softmax[b,j] - onehot) / denom.  denom is the local batch on
+ * one device or the global batch under data parallelism.  grad may be NULL.
+ * Replaces cuda_softmax_ce_forward_labels / _backward_labels
+ * (cuda_kernels.cu:1283-1374); NpArray semantics
+ * moonxi-net/nparray/image_impl.mbt:83-114,202-238. */
+int32_t mx_softmax_ce_labels(void* handle, const float* logits, const float* labels,
+                             float* grad, float* loss, int32_t batch, int32_t num_classes,
+                             int32_t denom, void* stream);
+
+/* Momentum SGD with global-norm auto clipping over one flat parameter
+ * buffer (all parameters concatenated in [w1, b1, w2, b2, ...] order):
+ *   norm = ||grads||, c = norm > max_norm ? max_norm / norm : 1,
+ *   v = momentum*v + g*c + weight_decay*p,  p = p - lr*v.
+ * Runs without a host round trip; norm_out (device, may be NULL) receives the
+ * norm.  Replaces mt_norm_sq + mt_sgd_momentum_autoclip (cuda_kernels.cu
+ * :1884-2029, driven by moonxi-net-gpu/tensor/optimizer.mbt:106-178). */
+int32_t mx_sgd_momentum_autoclip(void* handle, float* params, const float* grads, float* vels,
+                                 int64_t n, float lr, float momentum, float weight_decay,
+                                 float max_grad_norm, float* norm_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MX_MATMUL_H */

@@ -1,0 +1,458 @@
+// abi.cu -- the C-ABI layer (include/mx_matmul.h): contexts, argument
+// checking, precision dispatch and the exported entry points.
+//
+// The exported matmul keeps the reference's name, signature and semantics
+// (moonxi-net-gpu/cuda/cuda_kernels.cu:1464-1499 cuda_matmul and
+// moonxi-net-gpu/cuda/cuda_stub.c:948-969 moonbit_cuda_matmul): row-major,
+// transpose flags select the stored layout, C = alpha op(A) op(B) + beta C,
+// asynchronous on the stream, 0 on success.  Unlike the reference, invalid
+// arguments and in-kernel timeouts are reported as status codes instead of
+// being left to cuBLAS.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <unordered_set>
+
+#include "../../include/mx_matmul.h"
+#include "mx_internal.h"
+#include "mx_ptx.cuh"
+
+#define MX_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace mx {
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return kOk;
+  if (e == cudaErrorMemoryAllocation) return kErrNoMem;
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return kErrNoDevice;
+  return kErrCuda;
+}
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launches(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n)); }
+
+namespace {
+
+std::mutex g_mu;
+std::unordered_set<Context*> g_contexts;  // contexts handed out by mx_context_create
+Context* g_default[64] = {};              // per-device default contexts
+
+int env_precision() {
+  const char* e = std::getenv("MX_MATMUL_PRECISION");
+  if (!e) return MX_PREC_AUTO;
+  if (!strcmp(e, "fp32")) return MX_PREC_FP32;
+  if (!strcmp(e, "3xtf32")) return MX_PREC_3XTF32;
+  if (!strcmp(e, "tf32")) return MX_PREC_TF32;
+  return MX_PREC_AUTO;
+}
+
+int init_context(Context* c, int device) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return kErrNoDevice;
+  if (device < 0 || device >= count) return kErrInvalid;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  c->device = device;
+  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  c->precision = env_precision();
+  c->sync_check = std::getenv("MX_SYNC_CHECK") ? std::atoi(std::getenv("MX_SYNC_CHECK")) : 0;
+  cudaError_t e = cudaMalloc(&c->status, 2 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, 2 * sizeof(int));
+  if (prev != device) cudaSetDevice(prev);
+  return cuda_status(e);
+}
+
+// The context for `handle`: a registered context, else the current device's
+// default context (created on first use).  Never dereferences unknown handles.
+Context* resolve(void* handle) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Context* c = static_cast<Context*>(handle);
+  if (c && g_contexts.count(c)) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != c->device) cudaSetDevice(c->device);
+    return c;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!g_default[dev]) {
+    Context* d = new Context();
+    if (init_context(d, dev) != kOk) {
+      delete d;
+      return nullptr;
+    }
+    g_default[dev] = d;
+  }
+  return g_default[dev];
+}
+
+cudaStream_t pick_stream(Context* c, void* stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : c->stream;
+}
+
+int resolve_precision(Context* c, int M, int K, int N, int precision) {
+  int p = precision == MX_PREC_DEFAULT ? c->precision : precision;
+  if (p == MX_PREC_DEFAULT) p = MX_PREC_AUTO;
+  if (p == MX_PREC_AUTO) {
+    // Tensor cores pay off once the problem fills the machine; small or
+    // skinny products stay on the exact SIMT kernel.
+    const double flops = 2.0 * M * static_cast<double>(N) * K;
+    p = (M >= 128 && N >= 128 && K >= 64 && flops >= 1.0e9) ? MX_PREC_3XTF32 : MX_PREC_FP32;
+  }
+  return p;
+}
+
+int finish(Context* c, int rc, cudaStream_t s) {
+  if (rc != kOk || !c->sync_check) return rc;
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e);
+  int st[2] = {0, 0};
+  cudaMemcpy(st, c->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (st[0] != 0) {
+    cudaMemset(c->status, 0, sizeof(st));
+    return st[0];
+  }
+  return kOk;
+}
+
+int run_gemm(Context* c, const GemmArgs& g, int precision, cudaStream_t s) {
+  if (g.M < 0 || g.N < 0 || g.K < 0) return kErrInvalid;
+  if (g.M == 0 || g.N == 0) return kOk;
+  if (!g.c || ((!g.a || !g.b) && g.K > 0)) return kErrInvalid;
+  const int p = resolve_precision(c, g.M, g.K, g.N, precision);
+  int rc;
+  if (p == MX_PREC_3XTF32) rc = tc_gemm(c, g, 3, s);
+  else if (p == MX_PREC_TF32) rc = tc_gemm(c, g, 1, s);
+  else if (p == MX_PREC_FP32) rc = simt_gemm(c, g, s);
+  else rc = kErrInvalid;
+  return finish(c, rc, s);
+}
+
+GemmArgs ref_args(float* a, float* b, float* c, int M, int K, int N, int ta, int tb, float alpha,
+                  float beta) {
+  GemmArgs g;
+  g.a = a; g.b = b; g.c = c;
+  g.M = M; g.K = K; g.N = N;
+  g.ta = ta ? 1 : 0; g.tb = tb ? 1 : 0;
+  // Leading dimensions exactly as the reference derives them
+  // (cuda_kernels.cu:1482-1483): lda = ta ? M : K, ldb = tb ? K : N, ldc = N.
+  g.lda = ta ? M : K;
+  g.ldb = tb ? K : N;
+  g.ldc = N;
+  g.alpha = alpha; g.beta = beta;
+  return g;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  // Host-side checks of every TMA rule the hardware would otherwise trap on.
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if (row_stride_bytes % 16 != 0 || (box_inner * 4) % 16 != 0) return false;
+  if (box_inner > 256 || box_outer > 256 || inner == 0 || outer == 0) return false;
+  if (swizzle == CU_TENSOR_MAP_SWIZZLE_128B && box_inner * 4 > 128) return false;
+  if (swizzle == CU_TENSOR_MAP_SWIZZLE_64B && box_inner * 4 > 64) return false;
+  if (inner >= (1ull << 32) || outer >= (1ull << 32)) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int ensure_workspace(Context* c, size_t bytes) {
+  if (bytes <= c->ws_bytes) return kOk;
+  // Growth is rare (first call of a new largest shape); the old block may
+  // still be read by queued kernels, so drain the device before freeing it.
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e);
+  if (c->workspace) cudaFree(c->workspace);
+  c->workspace = nullptr;
+  c->ws_bytes = 0;
+  const size_t want = bytes + bytes / 8;
+  e = cudaMalloc(&c->workspace, want);
+  if (e != cudaSuccess) {
+    c->workspace = nullptr;
+    return kErrNoMem;
+  }
+  c->ws_bytes = want;
+  return kOk;
+}
+
+int ensure_small_scratch(Context* c, size_t bytes) {
+  if (bytes <= c->small_bytes) return kOk;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e);
+  if (c->small_scratch) cudaFree(c->small_scratch);
+  c->small_scratch = nullptr;
+  c->small_bytes = 0;
+  const size_t want = bytes < 65536 ? 65536 : bytes;
+  e = cudaMalloc(&c->small_scratch, want);
+  if (e != cudaSuccess) {
+    c->small_scratch = nullptr;
+    return kErrNoMem;
+  }
+  c->small_bytes = want;
+  return kOk;
+}
+
+}  // namespace mx
+
+using namespace mx;
+
+// ------------------------------------------------------------------ matmul
+MX_EXPORT int cuda_matmul(void* handle, float* a, float* b, float* c, int M, int K, int N,
+                          int transpose_a, int transpose_b, float alpha, float beta) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  return run_gemm(ctx, ref_args(a, b, c, M, K, N, transpose_a, transpose_b, alpha, beta),
+                  MX_PREC_DEFAULT, ctx->stream);
+}
+
+MX_EXPORT int32_t moonbit_cuda_matmul(void* handle, void* a, void* b, void* c, int32_t M,
+                                      int32_t K, int32_t N, int32_t transpose_a,
+                                      int32_t transpose_b, float alpha, float beta) {
+  return cuda_matmul(handle, static_cast<float*>(a), static_cast<float*>(b),
+                     static_cast<float*>(c), M, K, N, transpose_a, transpose_b, alpha, beta);
+}
+
+MX_EXPORT int32_t moonbit_cuda_matmul_ex(void* handle, void* a, void* b, void* c, int32_t M,
+                                         int32_t K, int32_t N, int32_t transpose_a,
+                                         int32_t transpose_b, float alpha, float beta,
+                                         void* stream, int32_t precision) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  return run_gemm(ctx,
+                  ref_args(static_cast<float*>(a), static_cast<float*>(b), static_cast<float*>(c),
+                           M, K, N, transpose_a, transpose_b, alpha, beta),
+                  precision, pick_stream(ctx, stream));
+}
+
+MX_EXPORT int32_t moonbit_cuda_linear_fwd_ex(void* handle, void* x, void* w, void* bias, void* y,
+                                             int32_t M, int32_t K, int32_t N,
+                                             int32_t transpose_w, int32_t relu, float alpha,
+                                             void* stream, int32_t precision) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  GemmArgs g = ref_args(static_cast<float*>(x), static_cast<float*>(w), static_cast<float*>(y), M,
+                        K, N, 0, transpose_w, alpha, 0.0f);
+  g.bias = static_cast<const float*>(bias);
+  g.relu = relu ? 1 : 0;
+  return run_gemm(ctx, g, precision, pick_stream(ctx, stream));
+}
+
+MX_EXPORT int32_t moonbit_cuda_linear_fwd(void* handle, void* x, void* w, void* bias, void* y,
+                                          int32_t M, int32_t K, int32_t N, int32_t transpose_w,
+                                          int32_t relu, float alpha) {
+  return moonbit_cuda_linear_fwd_ex(handle, x, w, bias, y, M, K, N, transpose_w, relu, alpha,
+                                    nullptr, MX_PREC_DEFAULT);
+}
+
+MX_EXPORT int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float* c,
+                             const float* bias, int32_t M, int32_t K, int32_t N,
+                             int32_t transpose_a, int32_t transpose_b, int64_t lda, int64_t ldb,
+                             int64_t ldc, float alpha, float beta, int32_t relu, void* stream,
+                             int32_t precision) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  GemmArgs g = ref_args(const_cast<float*>(a), const_cast<float*>(b), c, M, K, N, transpose_a,
+                        transpose_b, alpha, beta);
+  if (lda < 0 || ldb < 0 || ldc < 0) return MX_ERR_INVALID;
+  if (lda) g.lda = lda;
+  if (ldb) g.ldb = ldb;
+  if (ldc) g.ldc = ldc;
+  // A leading dimension smaller than the row it spans is an argument error.
+  if (g.lda < (g.ta ? M : K) || g.ldb < (g.tb ? K : N) || g.ldc < N) return MX_ERR_INVALID;
+  g.bias = bias;
+  g.relu = relu ? 1 : 0;
+  return run_gemm(ctx, g, precision, pick_stream(ctx, stream));
+}
+
+MX_EXPORT int32_t moonbit_cuda_set_device(int32_t device) {
+  return cuda_status(cudaSetDevice(device));
+}
+
+// ---------------------------------------------------------------- contexts
+MX_EXPORT void* mx_context_create(int32_t device) {
+  Context* c = new Context();
+  if (init_context(c, device) != kOk) {
+    delete c;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_contexts.insert(c);
+  return c;
+}
+
+MX_EXPORT void mx_context_destroy(void* handle) {
+  Context* c = static_cast<Context*>(handle);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!c || !g_contexts.count(c)) return;
+    g_contexts.erase(c);
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  if (c->workspace) cudaFree(c->workspace);
+  if (c->small_scratch) cudaFree(c->small_scratch);
+  if (c->status) cudaFree(c->status);
+  cudaSetDevice(prev);
+  delete c;
+}
+
+MX_EXPORT int32_t mx_context_set_stream(void* handle, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  c->stream = static_cast<cudaStream_t>(stream);
+  return MX_OK;
+}
+
+MX_EXPORT int32_t mx_context_set_precision(void* handle, int32_t precision) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (precision < MX_PREC_DEFAULT || precision > MX_PREC_TF32) return MX_ERR_INVALID;
+  c->precision = precision == MX_PREC_DEFAULT ? env_precision() : precision;
+  return MX_OK;
+}
+
+MX_EXPORT int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (ns == 0) return MX_ERR_INVALID;
+  c->timeout_ns = ns;
+  return MX_OK;
+}
+
+MX_EXPORT int32_t mx_context_reserve_workspace(void* handle, uint64_t bytes) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  int rc = ensure_workspace(c, bytes);
+  if (rc == kOk) rc = ensure_small_scratch(c, 1 << 20);
+  return rc;
+}
+
+MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K, int32_t N,
+                                             int32_t transpose_a, int32_t transpose_b,
+                                             int32_t precision) {
+  Context* c = resolve(handle);
+  if (!c || M <= 0 || N <= 0 || K < 0) return 0;
+  GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
+  const int p = resolve_precision(c, M, K, N, precision);
+  if (p == MX_PREC_3XTF32) return tc_gemm_workspace_bytes(g, 3);
+  if (p == MX_PREC_TF32) return tc_gemm_workspace_bytes(g, 1);
+  return simt_gemm_scratch_bytes(c, g);
+}
+
+MX_EXPORT int32_t mx_context_status(void* handle, int32_t* where) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e);
+  int st[2] = {0, 0};
+  e = cudaMemcpy(st, c->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (where) *where = st[1];
+  if (st[0] != 0) cudaMemset(c->status, 0, sizeof(st));
+  return st[0];
+}
+
+MX_EXPORT int32_t mx_matmul_resolve_precision(void* handle, int32_t M, int32_t K, int32_t N,
+                                              int32_t precision) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  return resolve_precision(c, M, K, N, precision);
+}
+
+MX_EXPORT const char* mx_status_string(int32_t status) {
+  switch (status) {
+    case MX_OK: return "ok";
+    case MX_ERR_INVALID: return "invalid argument";
+    case MX_ERR_UNSUPPORTED: return "unsupported shape or stride";
+    case MX_ERR_CUDA: return "CUDA runtime error";
+    case MX_ERR_TIMEOUT: return "bounded in-kernel wait timed out";
+    case MX_ERR_NOMEM: return "workspace allocation failed";
+    case MX_ERR_NO_DEVICE: return "no usable CUDA device";
+    default: return "unknown status";
+  }
+}
+
+MX_EXPORT uint64_t mx_kernel_launch_count(void) { return g_launches.load(); }
+
+// ------------------------------------------------------- training-step ops
+MX_EXPORT int32_t mx_relu_backward(void* handle, const float* grad_out, const float* saved,
+                                   float* grad_in, int64_t n, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (n < 0 || (n > 0 && (!grad_out || !saved || !grad_in))) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c, relu_backward(c, grad_out, saved, grad_in, n, s), s);
+}
+
+MX_EXPORT int32_t mx_reduce_sum_leading(void* handle, const float* in, float* out,
+                                        int32_t output_numel, int32_t lead_stride, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (output_numel < 0 || lead_stride < 0 || (output_numel > 0 && (!in || !out)))
+    return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c, reduce_sum_leading(c, in, out, output_numel, lead_stride, s), s);
+}
+
+MX_EXPORT int32_t mx_softmax_ce_labels(void* handle, const float* logits, const float* labels,
+                                       float* grad, float* loss, int32_t batch,
+                                       int32_t num_classes, int32_t denom, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (!logits || !labels || batch <= 0 || num_classes <= 0 || denom <= 0) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c, softmax_ce_labels(c, logits, labels, grad, loss, batch, num_classes, denom, s),
+                s);
+}
+
+MX_EXPORT int32_t mx_sgd_momentum_autoclip(void* handle, float* params, const float* grads,
+                                           float* vels, int64_t n, float lr, float momentum,
+                                           float weight_decay, float max_grad_norm,
+                                           float* norm_out, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (n < 0 || (n > 0 && (!params || !grads || !vels))) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c,
+                sgd_momentum_autoclip(c, params, grads, vels, n, lr, momentum, weight_decay,
+                                      max_grad_norm, norm_out, s),
+                s);
+}

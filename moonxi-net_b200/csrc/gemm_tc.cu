@@ -1,0 +1,428 @@
+// gemm_tc.cu -- tcgen05 / TMEM tensor-core GEMM for sm_100a, fp32-class by
+// 3xTF32 splitting (passes = 3) or plain TF32 (passes = 1).
+//
+// Replaces the cublasGemmEx call of the reference's cuda_matmul
+// (moonxi-net-gpu/cuda/cuda_kernels.cu:1464-1499) for large shapes.
+//
+// Split:  x = hi + lo with hi = rna_tf32(x), lo = rna_tf32(x - hi).  A
+// prepass writes hi/lo of each operand in K-major order ([rows][Kp], Kp = K
+// rounded up to 4 floats so TMA strides are 16-byte multiples); the prepass
+// reads the operand in whatever layout it is stored (ta/tb), so NN/NT/TN all
+// reach the tensor cores as K-major tiles.  The product accumulates
+//   lo_a*hi_b + hi_a*lo_b + hi_a*hi_b
+// per k-step in one fp32 TMEM accumulator (the lo*lo term, below 2^-22
+// relative, is dropped).
+//
+// Main kernel (persistent, one CTA per SM, 192 threads):
+//   warp 0     TMA producer: per k-block of 16, loads A_hi, A_lo (128x16) and
+//              B_hi, B_lo (256x16) with 64-byte swizzle into a 4-stage ring.
+//   warp 1     allocates 512 TMEM columns (two 128x256 fp32 accumulators),
+//              one lane issues tcgen05.mma kind::tf32 (M=128, N=256, K=8) and
+//              tcgen05.commit to free ring stages / publish accumulators.
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, alpha/beta/bias/
+//              ReLU, predicated stores.  Two accumulators let the epilogue of
+//              tile i overlap the main loop of tile i+1.
+// Every mbarrier wait is bounded (mx::wait_bar); a timeout raises a kernel
+// abort flag, records kErrTimeout, drains in-flight copies and MMAs, frees
+// TMEM and returns.
+#include <algorithm>
+
+#include "mx_internal.h"
+#include "mx_ptx.cuh"
+
+namespace mx {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 16;  // kBK fp32 = 64-byte rows
+constexpr int kATile = kBM * kBK * 4;           // 8 KB
+constexpr int kBTile = kBN * kBK * 4;           // 16 KB
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kSbo = 8 * kBK * 4;          // 8 rows x 64 B = 512 B
+constexpr uint32_t kLayoutSw64 = 4;
+
+template <int PASSES>
+struct Cfg {
+  static constexpr int kOperandCopies = PASSES == 3 ? 2 : 1;
+  static constexpr int kStageBytes = kOperandCopies * (kATile + kBTile);
+  static constexpr int kStages = PASSES == 3 ? 4 : 8;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+struct TcParams {
+  float* c;
+  const float* bias;
+  int* status;
+  int64_t ldc;
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  float alpha, beta;
+  int relu;
+  uint64_t timeout_ns;
+};
+
+// Grouped raster: bands of 16 M-tiles, N-major inside a band, so the CTAs
+// running at one time share A and B tiles in L2.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 16;
+  const int band = t / (G * tiles_n);
+  const int first_m = band * G;
+  const int gm = min(G, tiles_m - first_m);
+  const int r = t - band * G * tiles_n;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int PASSES>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                   const TcParams p) {
+  using C = Cfg<PASSES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* drain = acc_empty + 2;           // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      bar_init(&acc_full[a], 1);
+      bar_init(&acc_empty[a], 128);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmAh);
+    tma_prefetch_desc(&tmBh);
+    if (PASSES == 3) {
+      tma_prefetch_desc(&tmAl);
+      tma_prefetch_desc(&tmBl);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int armed_parity[C::kStages];
+      bool armed[C::kStages];
+      for (int s = 0; s < C::kStages; ++s) armed[s] = false;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(&empty[stage], phase ^ 1, abort_flag, p.status, p.timeout_ns, 201)) {
+            ok = false;
+            break;
+          }
+          uint8_t* base = smem + stage * C::kStageBytes;
+          bar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          armed[stage] = true;
+          armed_parity[stage] = phase;
+          const int k0 = kb * kBK;
+          tma_load_2d(base, &tmAh, &full[stage], k0, tm * kBM);
+          if (PASSES == 3) {
+            tma_load_2d(base + kATile, &tmAl, &full[stage], k0, tm * kBM);
+            tma_load_2d(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN);
+            tma_load_2d(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0, tn * kBN);
+          } else {
+            tma_load_2d(base + kATile, &tmBh, &full[stage], k0, tn * kBN);
+          }
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every copy this thread issued must land before the CTA can exit.
+      for (int s = 0; s < C::kStages; ++s) {
+        if (!armed[s]) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (!bar_try_wait(&full[s], armed_parity[s]) && globaltimer_ns() - t0 < p.timeout_ns) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(kBM, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_bar(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, p.timeout_ns, 202)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        uint32_t accumulate = 0;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(&full[stage], phase, abort_flag, p.status, p.timeout_ns, 203)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t s_base = smem_u32(smem + stage * C::kStageBytes);
+          const uint32_t s_ah = s_base;
+          const uint32_t s_al = s_base + kATile;
+          const uint32_t s_bh = s_base + (PASSES == 3 ? 2 * kATile : kATile);
+          const uint32_t s_bl = s_base + 2 * kATile + kBTile;
+#pragma unroll
+          for (int k8 = 0; k8 < kBK / 8; ++k8) {
+            const uint32_t koff = k8 * 32;  // 8 tf32 = 32 bytes along the swizzled row
+            const uint64_t ah = sdesc_kmajor(s_ah + koff, kSbo, kLayoutSw64);
+            const uint64_t bh = sdesc_kmajor(s_bh + koff, kSbo, kLayoutSw64);
+            if (PASSES == 3) {
+              const uint64_t al = sdesc_kmajor(s_al + koff, kSbo, kLayoutSw64);
+              const uint64_t bl = sdesc_kmajor(s_bl + koff, kSbo, kLayoutSw64);
+              mma_tf32(d_tmem, al, bh, idesc, accumulate);
+              mma_tf32(d_tmem, ah, bl, idesc, 1u);
+              mma_tf32(d_tmem, ah, bh, idesc, 1u);
+            } else {
+              mma_tf32(d_tmem, ah, bh, idesc, accumulate);
+            }
+            accumulate = 1u;
+          }
+          tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);  // accumulator ready for the epilogue
+      }
+      // Wait for every MMA this thread issued before TMEM is released.
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!bar_try_wait(drain, 0) && globaltimer_ns() - t0 < p.timeout_ns) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int lane_grp = warp & 3;                 // TMEM lanes this warp may access
+    const int row_in_tile = lane_grp * 32 + lane;
+    const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0);
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!wait_bar(&acc_full[acc], acc_phase, abort_flag, p.status, p.timeout_ns, 204)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int row = tm * kBM + row_in_tile;
+      float* crow = p.c + static_cast<int64_t>(row) * p.ldc;
+#pragma unroll 1
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * kBN +
+                           chunk * 32,
+                       r);
+        tmem_wait_ld();
+        const int col0 = tn * kBN + chunk * 32;
+        if (row < p.M && col0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = p.alpha * __uint_as_float(r[j]);
+          const int col = col0 + j;
+          if (col < p.N) {
+            if (p.beta != 0.0f) x = x + p.beta * crow[col];
+            if (p.bias) x = x + __ldg(p.bias + col);
+            if (p.relu) x = x > 0.0f ? x : 0.0f;
+          }
+          v[j] = x;
+        }
+        if (vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) crow[col0 + j] = v[j];
+        }
+        }
+      }
+      tc_fence_before();
+      bar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------- prepass
+// hi/lo split of an operand viewed as [R rows][K]; writes dst[r * Kp + k].
+// K-contiguous source: straight copy order.
+__global__ void split_kcontig_kernel(const float* __restrict__ src, int64_t ld, int R, int K,
+                                     int64_t Kp, float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t total = static_cast<int64_t>(R) * K;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / K, k = idx - r * K;
+    const float x = src[r * ld + k];
+    const uint32_t h = f32_to_tf32_rna(x);
+    hi[r * Kp + k] = __uint_as_float(h);
+    if (lo) lo[r * Kp + k] = __uint_as_float(f32_to_tf32_rna(x - __uint_as_float(h)));
+  }
+}
+
+// MN-contiguous source (element (r, k) at src[k * ld + r]): 32x32 transpose
+// through shared memory so both the reads and the writes are coalesced.
+__global__ void split_transpose_kernel(const float* __restrict__ src, int64_t ld, int R, int K,
+                                       int64_t Kp, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int k = k0 + ty + i, r = r0 + tx;
+    tile[ty + i][tx] = (k < K && r < R) ? src[static_cast<int64_t>(k) * ld + r] : 0.0f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int r = r0 + ty + i, k = k0 + tx;
+    if (r < R && k < K) {
+      const float x = tile[tx][ty + i];
+      const uint32_t h = f32_to_tf32_rna(x);
+      hi[static_cast<int64_t>(r) * Kp + k] = __uint_as_float(h);
+      if (lo) lo[static_cast<int64_t>(r) * Kp + k] =
+          __uint_as_float(f32_to_tf32_rna(x - __uint_as_float(h)));
+    }
+  }
+}
+
+cudaError_t launch_split(const float* src, int64_t ld, bool kcontig, int R, int K, int64_t Kp,
+                         float* hi, float* lo, int num_sms, cudaStream_t s) {
+  if (kcontig) {
+    const int64_t total = static_cast<int64_t>(R) * K;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, num_sms * 16));
+    split_kcontig_kernel<<<blocks, 256, 0, s>>>(src, ld, R, K, Kp, hi, lo);
+    note_launches(1);
+  } else {
+    dim3 grid((R + 31) / 32, (K + 31) / 32);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    split_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, R, K, Kp, hi, lo);
+    note_launches(1);
+  }
+  return cudaGetLastError();
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+template <int PASSES>
+cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+                      const CUtensorMap& bl, const TcParams& p, int grid, cudaStream_t s) {
+  auto kern = tc_gemm_kernel<PASSES>;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<PASSES>::kSmem);
+    if (e != cudaSuccess) return e;
+    configured |= 1u << (dev & 31);
+  }
+  kern<<<grid, kThreads, Cfg<PASSES>::kSmem, s>>>(ah, al, bh, bl, p);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Workspace bytes tc_gemm needs for the split operands of this shape.
+size_t tc_gemm_workspace_bytes(const GemmArgs& g, int passes) {
+  const size_t kp = (static_cast<size_t>(g.K) + 3) & ~static_cast<size_t>(3);
+  const size_t copies = passes == 3 ? 2 : 1;
+  return copies * (align256(static_cast<size_t>(g.M) * kp * 4) +
+                   align256(static_cast<size_t>(g.N) * kp * 4));
+}
+
+int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
+  if (g.M == 0 || g.N == 0) return kOk;
+  if (g.K == 0) return simt_gemm(ctx, g, s);
+  if (passes != 1 && passes != 3) return kErrInvalid;
+  const int64_t Kp = (static_cast<int64_t>(g.K) + 3) & ~static_cast<int64_t>(3);
+  int rc = ensure_workspace(ctx, tc_gemm_workspace_bytes(g, passes));
+  if (rc != kOk) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);
+  float* a_hi = reinterpret_cast<float*>(ws);
+  ws += align256(static_cast<size_t>(g.M) * Kp * 4);
+  float* b_hi = reinterpret_cast<float*>(ws);
+  ws += align256(static_cast<size_t>(g.N) * Kp * 4);
+  float* a_lo = nullptr;
+  float* b_lo = nullptr;
+  if (passes == 3) {
+    a_lo = reinterpret_cast<float*>(ws);
+    ws += align256(static_cast<size_t>(g.M) * Kp * 4);
+    b_lo = reinterpret_cast<float*>(ws);
+  }
+  cudaError_t e = launch_split(g.a, g.lda, g.ta == 0, g.M, g.K, Kp, a_hi, a_lo, ctx->num_sms, s);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = launch_split(g.b, g.ldb, g.tb != 0, g.N, g.K, Kp, b_hi, b_lo, ctx->num_sms, s);
+  if (e != cudaSuccess) return cuda_status(e);
+
+  CUtensorMap tah{}, tal{}, tbh{}, tbl{};
+  bool ok = make_tmap_2d(&tah, a_hi, g.K, g.M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+            make_tmap_2d(&tbh, b_hi, g.K, g.N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (passes == 3)
+    ok = ok && make_tmap_2d(&tal, a_lo, g.K, g.M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+         make_tmap_2d(&tbl, b_lo, g.K, g.N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B);
+  else {
+    tal = tah;
+    tbl = tbh;
+  }
+  if (!ok) return kErrUnsupported;
+
+  TcParams p{};
+  p.c = g.c; p.bias = g.bias; p.status = ctx->status; p.ldc = g.ldc;
+  p.M = g.M; p.N = g.N; p.K = g.K;
+  p.tiles_m = (g.M + kBM - 1) / kBM;
+  p.tiles_n = (g.N + kBN - 1) / kBN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.alpha = g.alpha; p.beta = g.beta; p.relu = g.relu;
+  p.timeout_ns = ctx->timeout_ns;
+  const int grid = std::min(p.num_tiles, ctx->num_sms);
+  e = passes == 3 ? launch_tc<3>(tah, tal, tbh, tbl, p, grid, s)
+                  : launch_tc<1>(tah, tal, tbh, tbl, p, grid, s);
+  return e == cudaSuccess ? kOk : cuda_status(e);
+}
+
+}  // namespace mx

@@ -1,0 +1,230 @@
+// mlp_ops.cu -- the non-GEMM steps of one Linear/MLP training step, written
+// so none of them needs a host round trip:
+//   relu_backward        (replaces cuDNN ReLU backward, cuda_kernels.cu:812-831)
+//   reduce_sum_leading   (bias gradient, replaces cuda_kernels.cu:1383-1406)
+//   softmax_ce_labels    (loss + dlogits in one pass, replaces :1283-1374)
+//   sgd_momentum_autoclip over one flat parameter buffer (replaces the
+//                        pointer-table mt_norm_sq / mt_sgd_momentum_autoclip,
+//                        cuda_kernels.cu:1884-2029)
+// Reductions use a fixed order (no atomics), so every result is
+// run-to-run deterministic.  Arithmetic that NpArray performs as separate
+// fp32 multiply and add uses __fmul_rn/__fadd_rn so nvcc cannot fuse it.
+#include <algorithm>
+
+#include "mx_internal.h"
+#include "mx_ptx.cuh"
+
+namespace mx {
+namespace {
+
+__global__ void relu_backward_kernel(const float* __restrict__ g, const float* __restrict__ x,
+                                     float* __restrict__ out, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t n4 = ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(x) |
+                       reinterpret_cast<uintptr_t>(out)) & 15u) == 0 ? n / 4 : 0;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += stride) {
+    const float4 gv = reinterpret_cast<const float4*>(g)[i];
+    const float4 xv = reinterpret_cast<const float4*>(x)[i];
+    float4 o;
+    o.x = xv.x > 0.0f ? gv.x : 0.0f;
+    o.y = xv.y > 0.0f ? gv.y : 0.0f;
+    o.z = xv.z > 0.0f ? gv.z : 0.0f;
+    o.w = xv.w > 0.0f ? gv.w : 0.0f;
+    reinterpret_cast<float4*>(out)[i] = o;
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += stride)
+    out[i] = x[i] > 0.0f ? g[i] : 0.0f;
+}
+
+// Column sums of in[rows][cols]: block = 32 columns x 8 row lanes; each
+// lane sums rows lane, lane+8, ... in order, then the 8 lane sums are added
+// in a fixed tree.
+__global__ void reduce_leading_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                      int cols, int rows) {
+  __shared__ float part[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + tx;
+  float s0 = 0.0f, s1 = 0.0f;
+  if (col < cols) {
+    int r = ty;
+    for (; r + 8 < rows; r += 16) {
+      s0 += in[static_cast<int64_t>(r) * cols + col];
+      s1 += in[static_cast<int64_t>(r + 8) * cols + col];
+    }
+    if (r < rows) s0 += in[static_cast<int64_t>(r) * cols + col];
+  }
+  part[ty][tx] = s0 + s1;
+  __syncthreads();
+  if (ty == 0 && col < cols) {
+    const float a = (part[0][tx] + part[1][tx]) + (part[2][tx] + part[3][tx]);
+    const float b = (part[4][tx] + part[5][tx]) + (part[6][tx] + part[7][tx]);
+    out[col] = a + b;
+  }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per row; 8 rows per block.  exp/log are evaluated in double and
+// rounded to float, as NpArray does (image_impl.mbt:95-103).  Writes the
+// block's partial loss (sum of its rows' -log p[label]) to partial[block].
+__global__ void softmax_ce_kernel(const float* __restrict__ logits,
+                                  const float* __restrict__ labels, float* __restrict__ grad,
+                                  float* __restrict__ partial, int batch, int C, float denom) {
+  __shared__ float row_loss[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  float loss = 0.0f;
+  if (b < batch) {
+    const float* row = logits + static_cast<int64_t>(b) * C;
+    const int label = static_cast<int>(labels[b]);
+    float mx_ = -INFINITY;
+    for (int j = lane; j < C; j += 32) mx_ = fmaxf(mx_, row[j]);
+    mx_ = warp_max(mx_);
+    float se = 0.0f;
+    for (int j = lane; j < C; j += 32)
+      se = __fadd_rn(se, static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))));
+    se = warp_sum(se);
+    const float lse = static_cast<float>(log(static_cast<double>(se)));
+    if (lane == 0) {
+      const float lp = __fsub_rn(__fsub_rn(row[label], mx_), lse);
+      loss = -lp;
+    }
+    if (grad) {
+      float* g = grad + static_cast<int64_t>(b) * C;
+      for (int j = lane; j < C; j += 32) {
+        const float sm =
+            __fdiv_rn(static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))), se);
+        const float t = (j == label) ? 1.0f : 0.0f;
+        g[j] = __fdiv_rn(__fsub_rn(sm, t), denom);
+      }
+    }
+  }
+  if (lane == 0) row_loss[warp] = loss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int w = 0; w < 8; ++w) s = __fadd_rn(s, row_loss[w]);
+    partial[blockIdx.x] = s;
+  }
+}
+
+// Sums n partials in a fixed order with one block; out[0] = sum / denom.
+__global__ void finish_sum_kernel(const float* __restrict__ partial, int n, float denom,
+                                  float* __restrict__ out, int write_sqrt) {
+  __shared__ float sh[256];
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < n; i += 256) s = __fadd_rn(s, partial[i]);
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) sh[threadIdx.x] = __fadd_rn(sh[threadIdx.x], sh[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float v = sh[0];
+    out[0] = write_sqrt ? __fsqrt_rn(v) : __fdiv_rn(v, denom);
+  }
+}
+
+// Per-block partial of sum g^2 over a grid-stride range (fixed grid -> fixed order).
+__global__ void norm_sq_kernel(const float* __restrict__ g, int64_t n, float* __restrict__ partial) {
+  __shared__ float sh[256];
+  float s = 0.0f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    s = __fadd_rn(s, __fmul_rn(g[i], g[i]));
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) sh[threadIdx.x] = __fadd_rn(sh[threadIdx.x], sh[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partial[blockIdx.x] = sh[0];
+}
+
+// v = momentum*v + g*clip + wd*p ; p = p - lr*v  (nparray/trait_impl.mbt:298-308).
+__global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                  float* __restrict__ v, int64_t n, float lr, float momentum,
+                                  float wd, float max_norm, const float* __restrict__ norm) {
+  const float nv = *norm;
+  const float clip = nv > max_norm ? __fdiv_rn(max_norm, nv) : 1.0f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+    const float cg = __fmul_rn(g[i], clip);
+    const float vn = __fadd_rn(__fadd_rn(__fmul_rn(momentum, v[i]), cg), __fmul_rn(wd, p[i]));
+    v[i] = vn;
+    p[i] = __fsub_rn(p[i], __fmul_rn(lr, vn));
+  }
+}
+
+int grid_for(int64_t n, int num_sms, int per_sm = 8) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, num_sms * per_sm)));
+}
+
+}  // namespace
+
+int relu_backward(Context* ctx, const float* g, const float* x, float* out, int64_t n,
+                  cudaStream_t s) {
+  if (n <= 0) return kOk;
+  relu_backward_kernel<<<grid_for((n + 3) / 4, ctx->num_sms), 256, 0, s>>>(g, x, out, n);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int rows,
+                       cudaStream_t s) {
+  if (cols <= 0) return kOk;
+  reduce_leading_kernel<<<(cols + 31) / 32, 256, 0, s>>>(in, out, cols, rows);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
+                      float* loss, int batch, int C, int denom, cudaStream_t s) {
+  if (batch <= 0 || C <= 0) return kErrInvalid;
+  const int blocks = (batch + 7) / 8;
+  int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks) * sizeof(float));
+  if (rc != kOk) return rc;
+  float* partial = static_cast<float*>(ctx->small_scratch);
+  softmax_ce_kernel<<<blocks, 256, 0, s>>>(logits, labels, grad, partial, batch, C,
+                                           static_cast<float>(denom));
+  note_launches(1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e);
+  if (loss) {
+    finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, static_cast<float>(denom), loss, 0);
+    note_launches(1);
+    e = cudaGetLastError();
+  }
+  return cuda_status(e);
+}
+
+int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
+                          float momentum, float wd, float max_norm, float* norm_out,
+                          cudaStream_t s) {
+  if (n <= 0) return kOk;
+  const int blocks = grid_for(n, ctx->num_sms, 4);
+  int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks + 1) * sizeof(float));
+  if (rc != kOk) return rc;
+  float* partial = static_cast<float*>(ctx->small_scratch);
+  float* norm = norm_out ? norm_out : partial + blocks;
+  norm_sq_kernel<<<blocks, 256, 0, s>>>(g, n, partial);
+  finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, 1.0f, norm, 1);
+  note_launches(3);  // norm_sq, finish_sum, sgd_update
+  sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
+                                                              max_norm, norm);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace mx

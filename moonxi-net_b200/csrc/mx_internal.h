@@ -1,0 +1,86 @@
+// mx_internal.h -- host-side declarations shared by the kernel files and the
+// C-ABI layer (abi.cu).  Nothing here is exported.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace mx {
+
+// Per-device execution context.  The reference passes an opaque handle to
+// every matmul (a cuBLAS handle, moonxi-net-gpu/cuda/gpu_context.mbt:67-71);
+// this library's handle is a Context, or NULL for the per-device default.
+struct Context {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;  // stream used by calls that take none
+  int precision = 0;              // MX_PREC_* default for calls that take none
+  int* status = nullptr;          // device words: [0] status code, [1] call site
+  void* workspace = nullptr;      // scratch for split operands / split-K partials
+  size_t ws_bytes = 0;
+  void* small_scratch = nullptr;  // reduction partials (loss, gradient norm)
+  size_t small_bytes = 0;
+  uint64_t timeout_ns = 2000000000ull;  // bound on every in-kernel wait
+  int sync_check = 0;             // synchronise and check status after each call
+};
+
+// One GEMM as the reference defines it (cuda_kernels.cu:1444-1499), with the
+// fused epilogue added: C = act(alpha * op(A) op(B) + beta * C + bias[col]).
+// Leading dimensions are in elements; ta/tb select the stored layout.
+struct GemmArgs {
+  const float* a = nullptr;
+  const float* b = nullptr;
+  float* c = nullptr;
+  int M = 0, K = 0, N = 0;
+  int ta = 0, tb = 0;
+  int64_t lda = 0, ldb = 0, ldc = 0;
+  float alpha = 1.0f, beta = 0.0f;
+  const float* bias = nullptr;
+  int relu = 0;
+};
+
+// Grows ctx->workspace to at least `bytes` (stream-ordered free of the old
+// block is not needed: growth synchronises the device first).
+int ensure_workspace(Context* ctx, size_t bytes);
+int ensure_small_scratch(Context* ctx, size_t bytes);
+
+// Exact-fp32 SIMT GEMM (FFMA), TMA-fed when strides allow, cp.async-fed
+// otherwise.  Uses ctx workspace for split-K partials.
+int simt_gemm(Context* ctx, const GemmArgs& g, cudaStream_t s);
+// Launch step of simt_gemm with the split-K scratch given explicitly
+// (`scratch` may be NULL when the plan needs none).  Never allocates.
+int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scratch,
+                     size_t scratch_bytes);
+// Bytes of split-K scratch simt_gemm would use for this shape on this device.
+size_t simt_gemm_scratch_bytes(const Context* ctx, const GemmArgs& g);
+
+// tcgen05 tensor-core GEMM.  passes = 3: 3xTF32 split (fp32-class);
+// passes = 1: plain TF32.  Uses ctx workspace for the split operands.
+int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s);
+
+size_t tc_gemm_workspace_bytes(const GemmArgs& g, int passes);
+
+// Adjacent ops of the training step (mlp_ops.cu).
+int relu_backward(Context* ctx, const float* g, const float* x, float* out, int64_t n,
+                  cudaStream_t s);
+int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int rows,
+                       cudaStream_t s);
+int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
+                      float* loss, int batch, int C, int denom, cudaStream_t s);
+int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
+                          float momentum, float wd, float max_norm, float* norm_out,
+                          cudaStream_t s);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle);
+
+int cuda_status(cudaError_t e);
+
+// Counts kernel launches (diagnostic, exported as mx_kernel_launch_count).
+void note_launches(int n);
+
+}  // namespace mx

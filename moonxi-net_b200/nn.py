@@ -1,0 +1,237 @@
+"""Linear/MLP training on the B200 matmul path, data-parallel across GPUs.
+
+This mirrors one training step of the reference (``Experiment::train_step``,
+moonxi-net/train/train.mbt:40-54, driven by ``run_gpu``,
+moonxi-net-gpu/train/run.mbt:41-57) for a stack of Linear layers with ReLU
+between them, cross-entropy with integer labels and momentum SGD with
+global-norm clipping.  The arithmetic follows the reference's autograd tape:
+
+* forward per layer ``x.matmul(w).add(b)`` then ``relu`` (layers.mbt:59-64;
+  layout "nn", w stored [in, out]) or ``x.matmul(w.transpose())``
+  (mlp.mbt:16-23; layout "nt", w stored [out, in]) -- one fused
+  ``moonbit_cuda_linear_fwd`` call (GEMM + broadcast bias + ReLU epilogue);
+* backward closures of grad/blas.mbt:23-39 (dW = X^T dY, dX = dY W^T, run as
+  TN / NT GEMMs on the stored operands, no transpose materialised),
+  grad/grad.mbt:163-174 (db = column sum) and grad/image.mbt:45-61 (ReLU
+  mask); the first layer's dX is skipped because the input has no gradient
+  (grad/grad.mbt:80-85);
+* update: momentum SGD with auto clipping (nparray/trait_impl.mbt:280-311)
+  over one flat parameter buffer, on the device, with no host round trip.
+
+Data parallelism (new; the reference has none): the batch is split by rows
+over the ranks of a ``torch.distributed`` process group; the loss is scaled by
+1/global_batch so the sum over ranks equals the single-device mean; each
+layer's (dW, db) bucket is all-reduced (NCCL over NVLink) as soon as its
+GEMMs are queued, so the reduction of layer i overlaps the backward GEMMs of
+layers i-1..1; every replica then applies the identical update.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import ops
+
+_ALIGN = 64  # floats: every parameter block starts on a 256-byte boundary
+_LOSS_SLOTS = _ALIGN  # the per-step loss rides in front of the first bucket
+
+
+def _round_up(x: int, a: int = _ALIGN) -> int:
+    return (x + a - 1) // a * a
+
+
+class MLP:
+    """A stack of Linear layers (ReLU between them) trained with momentum SGD.
+
+    Parameters live in one flat device buffer in the reference's parameter
+    order [w1, b1, w2, b2, ...]; gradients and velocities use the same layout.
+    """
+
+    def __init__(self, dims, weights=None, biases=None, layout: str = "nn", device=None,
+                 precision="default", lr: float = 0.01, momentum: float = 0.9,
+                 weight_decay: float = 1e-4, max_grad_norm: float = 35.0,
+                 process_group=None):
+        if layout not in ("nn", "nt"):
+            raise ValueError("layout must be 'nn' (w [in,out]) or 'nt' (w [out,in])")
+        self.dims = list(dims)
+        self.L = len(dims) - 1
+        self.layout = layout
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.precision = precision
+        self.lr, self.momentum = float(lr), float(momentum)
+        self.weight_decay, self.max_grad_norm = float(weight_decay), float(max_grad_norm)
+        self.pg = process_group
+        if process_group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(process_group)
+        else:
+            self.world = 1
+
+        # flat layout
+        self.w_off, self.b_off = [], []
+        off = 0
+        for i in range(self.L):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            self.w_off.append(off)
+            off += _round_up(fi * fo)
+            self.b_off.append(off)
+            off += _round_up(fo)
+        self.n_flat = off
+        dev = self.device
+        self.params = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+        self.vels = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+        # grads_buf = [loss slot (64 floats)] + grads (n_flat)
+        self.grads_buf = torch.zeros(_LOSS_SLOTS + self.n_flat, device=dev, dtype=torch.float32)
+        self.grads = self.grads_buf[_LOSS_SLOTS:]
+        self.loss_slot = self.grads_buf[:1]
+        self.norm = torch.zeros(1, device=dev, dtype=torch.float32)
+        self.w = [self._view(self.params, i, True) for i in range(self.L)]
+        self.b = [self._view(self.params, i, False) for i in range(self.L)]
+        self.gw = [self._view(self.grads, i, True) for i in range(self.L)]
+        self.gb = [self._view(self.grads, i, False) for i in range(self.L)]
+        if weights is not None:
+            self.load(weights, biases)
+        self._bufs = {}
+        self._graph = None
+        # optional list; when set, each GEMM of step() appends
+        # (algorithmic flops, start event, end event) -- used by the benchmark
+        self.gemm_timer = None
+
+    # ------------------------------------------------------------------ state
+    def _wshape(self, i):
+        fi, fo = self.dims[i], self.dims[i + 1]
+        return (fi, fo) if self.layout == "nn" else (fo, fi)
+
+    def _view(self, flat, i, is_w):
+        if is_w:
+            s = self._wshape(i)
+            return flat[self.w_off[i]:self.w_off[i] + s[0] * s[1]].view(s)
+        fo = self.dims[i + 1]
+        return flat[self.b_off[i]:self.b_off[i] + fo]
+
+    def load(self, weights, biases=None):
+        for i in range(self.L):
+            self.w[i].copy_(torch.as_tensor(np.asarray(weights[i], np.float32)).view(self._wshape(i)))
+            if biases is not None:
+                self.b[i].copy_(torch.as_tensor(np.asarray(biases[i], np.float32)))
+        self.vels.zero_()
+
+    def weights_numpy(self):
+        return ([w.detach().cpu().numpy().copy() for w in self.w],
+                [b.detach().cpu().numpy().copy() for b in self.b])
+
+    def grads_numpy(self):
+        out = []
+        for i in range(self.L):
+            out += [self.gw[i].detach().cpu().numpy().copy(),
+                    self.gb[i].detach().cpu().numpy().copy()]
+        return out
+
+    def bucket(self, i):
+        """Flat slice of grads_buf holding layer i's (dW, db); bucket 0 also
+        carries the loss slot."""
+        start = self.w_off[i] + _LOSS_SLOTS if i > 0 else 0
+        end = _LOSS_SLOTS + (self.w_off[i + 1] if i + 1 < self.L else self.n_flat)
+        return self.grads_buf[start:end]
+
+    def _buffers(self, B):
+        bufs = self._bufs.get(B)
+        if bufs is None:
+            dev = self.device
+            acts = [torch.empty((B, self.dims[i + 1]), device=dev, dtype=torch.float32)
+                    for i in range(self.L)]
+            gbuf = [torch.empty((B, self.dims[i + 1]), device=dev, dtype=torch.float32)
+                    for i in range(self.L)]
+            bufs = (acts, gbuf)
+            self._bufs[B] = bufs
+        return bufs
+
+    # ------------------------------------------------------------------ step
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        acts, _ = self._buffers(x.shape[0])
+        h = x
+        for i in range(self.L):
+            h = ops.linear(h, self.w[i], self.b[i], relu=(i + 1 < self.L),
+                           transpose_w=(self.layout == "nt"), out=acts[i],
+                           precision=self.precision)
+        return h
+
+    def step(self, x: torch.Tensor, labels: torch.Tensor, global_batch: int | None = None,
+             update: bool = True) -> torch.Tensor:
+        """One training step on this rank's rows; returns the (global) loss
+        as a 1-element device tensor."""
+        B = x.shape[0]
+        G = B * self.world if global_batch is None else int(global_batch)
+        acts, gbuf = self._buffers(B)
+        nt = self.layout == "nt"
+        prec = self.precision
+        timer = self.gemm_timer
+
+        def timed(flops, fn, *a, **k):
+            if timer is None:
+                return fn(*a, **k)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*a, **k)
+            e1.record()
+            timer.append((flops, e0, e1))
+            return r
+
+        # forward (fused GEMM + bias + ReLU per layer)
+        h = [x]
+        for i in range(self.L):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            timed(2 * B * fi * fo, ops.linear, h[i], self.w[i], self.b[i],
+                  relu=(i + 1 < self.L), transpose_w=nt, out=acts[i], precision=prec)
+            h.append(acts[i])
+        # loss and dlogits in one pass; the loss lands in the first bucket
+        ops.softmax_ce_labels(h[self.L], labels, denom=G, grad=gbuf[self.L - 1],
+                              loss=self.loss_slot)
+        works = []
+        g = gbuf[self.L - 1]
+        for i in reversed(range(self.L)):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            ops.reduce_sum_leading(g, out=self.gb[i])
+            if nt:   # dW[out,in] = dY^T X
+                timed(2 * B * fi * fo, ops.matmul, g, h[i], fo, B, fi, ta=True, tb=False,
+                      out=self.gw[i], precision=prec)
+            else:    # dW[in,out] = X^T dY
+                timed(2 * B * fi * fo, ops.matmul, h[i], g, fi, B, fo, ta=True, tb=False,
+                      out=self.gw[i], precision=prec)
+            if self.pg is not None:
+                import torch.distributed as dist
+                works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
+            if i > 0:
+                gprev = gbuf[i - 1]
+                # dX = dY W^T: w [in,out] -> stored [N=in, K=out] (tb=1); w [out,in] -> tb=0
+                timed(2 * B * fi * fo, ops.matmul, g, self.w[i], B, fo, fi, ta=False,
+                      tb=not nt, out=gprev, precision=prec)
+                ops.relu_backward(gprev, h[i], out=gprev)
+                g = gprev
+        for wk in works:
+            wk.wait()
+        if update:
+            ops.sgd_momentum_autoclip(self.params, self.grads, self.vels, self.lr, self.momentum,
+                                      self.weight_decay, self.max_grad_norm, norm_out=self.norm)
+        return self.loss_slot
+
+    # ------------------------------------------------------------ CUDA graph
+    def capture(self, x: torch.Tensor, labels: torch.Tensor, global_batch: int | None = None):
+        """Captures one full step (including the all-reduces) into a CUDA
+        graph reading from the given input buffers.  Run a step eagerly first
+        so every workspace is sized."""
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step(x, labels, global_batch)
+        self._graph = g
+        return g
+
+    def replay(self):
+        self._graph.replay()
+        return self.loss_slot
+
+    def release_graph(self):
+        self._graph = None

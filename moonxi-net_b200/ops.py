@@ -1,0 +1,195 @@
+"""Device ops of the matmul path, called through the C ABI.
+
+torch is used only for device memory and streams: every function here takes
+CUDA float32 tensors, passes their raw pointers and the current torch stream
+to ``libmxgemm.so`` and lets the library's kernels do the work.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import PRECISIONS, check
+
+_ctx_cache: dict[int, int] = {}
+
+
+def context(device: int | None = None) -> int:
+    """The library context (the ABI's ``handle``) for a device, created once."""
+    if device is None:
+        device = torch.cuda.current_device()
+    h = _ctx_cache.get(device)
+    if h is None:
+        h = _lib.lib().mx_context_create(device)
+        if not h:
+            raise _lib.MXError(_lib.MX_ERR_NO_DEVICE, f"mx_context_create({device})")
+        _ctx_cache[device] = h
+    return h
+
+
+def _prec(precision) -> int:
+    if isinstance(precision, str):
+        return PRECISIONS[precision]
+    return int(precision)
+
+
+def _stream_ptr(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _check_tensor(t: torch.Tensor, name: str, numel: int | None = None):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if numel is not None and t.numel() < numel:
+        raise ValueError(f"{name} has {t.numel()} elements, needs {numel}")
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = False,
+           tb: bool = False, alpha: float = 1.0, beta: float = 0.0,
+           out: torch.Tensor | None = None, precision="default", stream=None) -> torch.Tensor:
+    """C[M,N] = alpha op(A) op(B) + beta C (the reference's cuda_matmul)."""
+    _check_tensor(a, "a", M * K)
+    _check_tensor(b, "b", K * N)
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=torch.float32)
+    _check_tensor(out, "out", M * N)
+    rc = _lib.lib().moonbit_cuda_matmul_ex(
+        context(a.device.index), a.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, int(ta),
+        int(tb), float(alpha), float(beta), _stream_ptr(stream), _prec(precision))
+    check(rc, "moonbit_cuda_matmul_ex")
+    return out
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = False,
+         tb: bool = False, alpha: float = 1.0, beta: float = 0.0,
+         bias: torch.Tensor | None = None, relu: bool = False,
+         out: torch.Tensor | None = None, precision="default", stream=None,
+         lda: int = 0, ldb: int = 0, ldc: int = 0) -> torch.Tensor:
+    """C = act(alpha op(A) op(B) + beta C + bias) for any layout (mx_gemm_ex)."""
+    _check_tensor(a, "a", M * K if not lda else 1)
+    _check_tensor(b, "b", K * N if not ldb else 1)
+    if bias is not None:
+        _check_tensor(bias, "bias", N)
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=torch.float32)
+    _check_tensor(out, "out", M * N if not ldc else 1)
+    rc = _lib.lib().mx_gemm_ex(
+        context(a.device.index), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+        bias.data_ptr() if bias is not None else None, M, K, N, int(ta), int(tb), int(lda),
+        int(ldb), int(ldc), float(alpha), float(beta), int(relu), _stream_ptr(stream),
+        _prec(precision))
+    check(rc, "mx_gemm_ex")
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, relu: bool = False,
+           transpose_w: bool = False, out: torch.Tensor | None = None, alpha: float = 1.0,
+           precision="default", stream=None) -> torch.Tensor:
+    """y = act(alpha x op(w) + bias): w is [K,N] (transpose_w=False) or [N,K]."""
+    M, K = x.shape
+    N = w.shape[0] if transpose_w else w.shape[1]
+    _check_tensor(x, "x")
+    _check_tensor(w, "w", K * N)
+    if bias is not None:
+        _check_tensor(bias, "bias", N)
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.float32)
+    _check_tensor(out, "out", M * N)
+    rc = _lib.lib().moonbit_cuda_linear_fwd_ex(
+        context(x.device.index), x.data_ptr(), w.data_ptr(),
+        bias.data_ptr() if bias is not None else None, out.data_ptr(), M, K, N,
+        int(transpose_w), int(relu), float(alpha), _stream_ptr(stream), _prec(precision))
+    check(rc, "moonbit_cuda_linear_fwd_ex")
+    return out
+
+
+def relu_backward(grad_out: torch.Tensor, saved: torch.Tensor, out: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+    _check_tensor(grad_out, "grad_out")
+    _check_tensor(saved, "saved", grad_out.numel())
+    if out is None:
+        out = torch.empty_like(grad_out)
+    _check_tensor(out, "out", grad_out.numel())
+    rc = _lib.lib().mx_relu_backward(context(grad_out.device.index), grad_out.data_ptr(),
+                                     saved.data_ptr(), out.data_ptr(), grad_out.numel(),
+                                     _stream_ptr(stream))
+    check(rc, "mx_relu_backward")
+    return out
+
+
+def reduce_sum_leading(x: torch.Tensor, out: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+    """Column sums of a [rows, cols] tensor (the bias gradient)."""
+    rows, cols = x.shape
+    _check_tensor(x, "x")
+    if out is None:
+        out = torch.empty((cols,), device=x.device, dtype=torch.float32)
+    _check_tensor(out, "out", cols)
+    rc = _lib.lib().mx_reduce_sum_leading(context(x.device.index), x.data_ptr(), out.data_ptr(),
+                                          cols, rows, _stream_ptr(stream))
+    check(rc, "mx_reduce_sum_leading")
+    return out
+
+
+def softmax_ce_labels(logits: torch.Tensor, labels: torch.Tensor, denom: int | None = None,
+                      grad: torch.Tensor | None = None, loss: torch.Tensor | None = None,
+                      want_grad: bool = True, stream=None):
+    """(loss[1], dlogits) of mean cross-entropy with float class labels."""
+    B, C = logits.shape
+    _check_tensor(logits, "logits")
+    _check_tensor(labels, "labels", B)
+    if loss is None:
+        loss = torch.empty((1,), device=logits.device, dtype=torch.float32)
+    if want_grad and grad is None:
+        grad = torch.empty_like(logits)
+    rc = _lib.lib().mx_softmax_ce_labels(
+        context(logits.device.index), logits.data_ptr(), labels.data_ptr(),
+        grad.data_ptr() if want_grad else None, loss.data_ptr(), B, C,
+        B if denom is None else int(denom), _stream_ptr(stream))
+    check(rc, "mx_softmax_ce_labels")
+    return loss, grad
+
+
+def sgd_momentum_autoclip(params: torch.Tensor, grads: torch.Tensor, vels: torch.Tensor, lr: float,
+                          momentum: float, weight_decay: float, max_grad_norm: float,
+                          norm_out: torch.Tensor | None = None, n: int | None = None,
+                          stream=None) -> None:
+    n = params.numel() if n is None else n
+    for t, name in ((params, "params"), (grads, "grads"), (vels, "vels")):
+        _check_tensor(t, name, n)
+    rc = _lib.lib().mx_sgd_momentum_autoclip(
+        context(params.device.index), params.data_ptr(), grads.data_ptr(), vels.data_ptr(), n,
+        float(lr), float(momentum), float(weight_decay), float(max_grad_norm),
+        norm_out.data_ptr() if norm_out is not None else None, _stream_ptr(stream))
+    check(rc, "mx_sgd_momentum_autoclip")
+
+
+def status(device: int | None = None) -> tuple[int, int]:
+    """(status, call site) of the device status word; synchronises, clears it."""
+    where = ctypes.c_int32(0)
+    rc = _lib.lib().mx_context_status(context(device), ctypes.byref(where))
+    return rc, where.value
+
+
+def reserve_workspace(nbytes: int, device: int | None = None) -> None:
+    check(_lib.lib().mx_context_reserve_workspace(context(device), int(nbytes)),
+          "mx_context_reserve_workspace")
+
+
+def workspace_bytes(M: int, K: int, N: int, ta=False, tb=False, precision="default",
+                    device: int | None = None) -> int:
+    return int(_lib.lib().mx_matmul_workspace_bytes(context(device), M, K, N, int(ta), int(tb),
+                                                    _prec(precision)))
+
+
+def resolve_precision(M: int, K: int, N: int, precision="default",
+                      device: int | None = None) -> str:
+    p = _lib.lib().mx_matmul_resolve_precision(context(device), M, K, N, _prec(precision))
+    return {v: k for k, v in PRECISIONS.items()}[p]

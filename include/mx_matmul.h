@@ -42,6 +42,9 @@ extern "C" {
 #define MX_PREC_FP32 2    /* exact-fp32 SIMT (FFMA) kernel                     */
 #define MX_PREC_3XTF32 3  /* tcgen05 3xTF32 split, fp32-class accuracy         */
 #define MX_PREC_TF32 4    /* tcgen05 plain TF32 (opt-in, ~1e-3 relative)       */
+#define MX_PREC_NPARRAY 5 /* bit-exact to the NpArray CPU path: fp32 multiply then add in
+                           * k order, no split-K (SIMT, half the FP32 rate).  On a
+                           * context it also puts the training-step ops in NpArray order. */
 
 /* ---------------------------------------------------------------------- */
 /* Reference-compatible entry points                                       */

@@ -28,8 +28,9 @@ PREC_AUTO = 1
 PREC_FP32 = 2
 PREC_3XTF32 = 3
 PREC_TF32 = 4
+PREC_NPARRAY = 5
 PRECISIONS = {"default": PREC_DEFAULT, "auto": PREC_AUTO, "fp32": PREC_FP32,
-              "3xtf32": PREC_3XTF32, "tf32": PREC_TF32}
+              "3xtf32": PREC_3XTF32, "tf32": PREC_TF32, "nparray": PREC_NPARRAY}
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32

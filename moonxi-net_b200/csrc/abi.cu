@@ -48,6 +48,7 @@ int env_precision() {
   if (!strcmp(e, "fp32")) return MX_PREC_FP32;
   if (!strcmp(e, "3xtf32")) return MX_PREC_3XTF32;
   if (!strcmp(e, "tf32")) return MX_PREC_TF32;
+  if (!strcmp(e, "nparray")) return MX_PREC_NPARRAY;
   return MX_PREC_AUTO;
 }
 
@@ -130,7 +131,11 @@ int run_gemm(Context* c, const GemmArgs& g, int precision, cudaStream_t s) {
   if (p == MX_PREC_3XTF32) rc = tc_gemm(c, g, 3, s);
   else if (p == MX_PREC_TF32) rc = tc_gemm(c, g, 1, s);
   else if (p == MX_PREC_FP32) rc = simt_gemm(c, g, s);
-  else rc = kErrInvalid;
+  else if (p == MX_PREC_NPARRAY) {
+    GemmArgs gs = g;
+    gs.strict = 1;
+    rc = simt_gemm(c, gs, s);
+  } else rc = kErrInvalid;
   return finish(c, rc, s);
 }
 
@@ -344,7 +349,7 @@ MX_EXPORT int32_t mx_context_set_stream(void* handle, void* stream) {
 MX_EXPORT int32_t mx_context_set_precision(void* handle, int32_t precision) {
   Context* c = resolve(handle);
   if (!c) return MX_ERR_NO_DEVICE;
-  if (precision < MX_PREC_DEFAULT || precision > MX_PREC_TF32) return MX_ERR_INVALID;
+  if (precision < MX_PREC_DEFAULT || precision > MX_PREC_NPARRAY) return MX_ERR_INVALID;
   c->precision = precision == MX_PREC_DEFAULT ? env_precision() : precision;
   return MX_OK;
 }
@@ -374,6 +379,7 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
   const int p = resolve_precision(c, M, K, N, precision);
   if (p == MX_PREC_3XTF32) return tc_gemm_workspace_bytes(g, 3);
   if (p == MX_PREC_TF32) return tc_gemm_workspace_bytes(g, 1);
+  if (p == MX_PREC_NPARRAY) return 0;  // no split-K in NpArray order
   return simt_gemm_scratch_bytes(c, g);
 }
 

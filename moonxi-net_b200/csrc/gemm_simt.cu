@@ -95,7 +95,11 @@ __device__ __forceinline__ int own_index(int t, int i) {
   return KC ? t + 16 * i : ((i < 4) ? t * 4 + i : 64 + t * 4 + (i - 4));
 }
 
-template <bool AK, bool BKC>
+// STRICT: every output is the NpArray sum -- fp32 product rounded, then
+// added, k ascending (nparray/trait_impl.mbt:236-241) -- so the result is
+// bit-identical to the CPU path (half the FFMA rate).  Otherwise fused
+// multiply-add, k ascending.
+template <bool AK, bool BKC, bool STRICT>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ sA,
                                               const float* __restrict__ sB, int ty, int tx,
                                               float (&acc)[8][8]) {
@@ -141,11 +145,14 @@ __device__ __forceinline__ void compute_stage(const float* __restrict__ sA,
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i][kk], b[j][kk], acc[i][j]);
+        for (int j = 0; j < 8; ++j) {
+          if (STRICT) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i][kk], b[j][kk]));
+          else        acc[i][j] = fmaf(a[i][kk], b[j][kk], acc[i][j]);
+        }
   }
 }
 
-template <bool AK, bool BKC, bool TMA>
+template <bool AK, bool BKC, bool TMA, bool STRICT>
 __global__ void __launch_bounds__(kThreads, 1)
     simt_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const SimtParams p) {
@@ -201,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = it % kStages;
       const bool ok = wait_bar(&full[s], (it / kStages) & 1, abort_flag, p.status,
                                p.timeout_ns, 101);
-      if (ok) compute_stage<AK, BKC>(smem + s * 2 * kTileFloats,
+      if (ok) compute_stage<AK, BKC, STRICT>(smem + s * 2 * kTileFloats,
                                      smem + s * 2 * kTileFloats + kTileFloats, ty, tx, acc);
       if (__syncthreads_or(!ok)) { aborted = true; break; }
       if (tid == 0 && it + kStages < nkb) issue(it + kStages);
@@ -241,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       cp_async_commit();
       const int s = it % kStages;
-      compute_stage<AK, BKC>(smem + s * 2 * kTileFloats,
+      compute_stage<AK, BKC, STRICT>(smem + s * 2 * kTileFloats,
                              smem + s * 2 * kTileFloats + kTileFloats, ty, tx, acc);
     }
     cp_async_wait<0>();
@@ -300,10 +307,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, float* c
   }
 }
 
-template <bool AK, bool BKC, bool TMA>
+template <bool AK, bool BKC, bool TMA, bool STRICT>
 cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const SimtParams& p,
                            dim3 grid, cudaStream_t s) {
-  auto kern = simt_gemm_kernel<AK, BKC, TMA>;
+  auto kern = simt_gemm_kernel<AK, BKC, TMA, STRICT>;
   static unsigned configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -318,9 +325,23 @@ cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const S
   return cudaGetLastError();
 }
 
+template <bool TMA, bool STRICT>
+cudaError_t dispatch_layout(bool ak, bool bkc, const CUtensorMap& ta, const CUtensorMap& tb,
+                            const SimtParams& p, dim3 grid, cudaStream_t s) {
+  if (ak && bkc) return launch_variant<true, true, TMA, STRICT>(ta, tb, p, grid, s);
+  if (ak) return launch_variant<true, false, TMA, STRICT>(ta, tb, p, grid, s);
+  if (bkc) return launch_variant<false, true, TMA, STRICT>(ta, tb, p, grid, s);
+  return launch_variant<false, false, TMA, STRICT>(ta, tb, p, grid, s);
+}
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 void plan_splits(const Context* ctx, const GemmArgs& g, int* splits, int* kb_per_split) {
+  if (g.strict) {  // one pass over k in order: no split-K
+    *splits = 1;
+    *kb_per_split = std::max(1, (g.K + kBK - 1) / kBK);
+    return;
+  }
   const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + kBN - 1) / kBN);
   const int num_kb = (g.K + kBK - 1) / kBK;
   int sp = 1;
@@ -379,16 +400,12 @@ int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scr
   dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM, p.splits);
   if (grid.y > 65535) return kErrUnsupported;
   cudaError_t e;
-  if (use_tma) {
-    if (ak && bkc) e = launch_variant<true, true, true>(ta, tb, p, grid, s);
-    else if (ak) e = launch_variant<true, false, true>(ta, tb, p, grid, s);
-    else if (bkc) e = launch_variant<false, true, true>(ta, tb, p, grid, s);
-    else e = launch_variant<false, false, true>(ta, tb, p, grid, s);
+  if (g.strict) {
+    if (use_tma) e = dispatch_layout<true, true>(ak, bkc, ta, tb, p, grid, s);
+    else         e = dispatch_layout<false, true>(ak, bkc, ta, tb, p, grid, s);
   } else {
-    if (ak && bkc) e = launch_variant<true, true, false>(ta, tb, p, grid, s);
-    else if (ak) e = launch_variant<true, false, false>(ta, tb, p, grid, s);
-    else if (bkc) e = launch_variant<false, true, false>(ta, tb, p, grid, s);
-    else e = launch_variant<false, false, false>(ta, tb, p, grid, s);
+    if (use_tma) e = dispatch_layout<true, false>(ak, bkc, ta, tb, p, grid, s);
+    else         e = dispatch_layout<false, false>(ak, bkc, ta, tb, p, grid, s);
   }
   if (e != cudaSuccess) return cuda_status(e);
   if (p.splits > 1) {

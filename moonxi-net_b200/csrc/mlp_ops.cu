@@ -11,6 +11,7 @@
 // fp32 multiply and add uses __fmul_rn/__fadd_rn so nvcc cannot fuse it.
 #include <algorithm>
 
+#include "../../include/mx_matmul.h"
 #include "mx_internal.h"
 #include "mx_ptx.cuh"
 
@@ -168,6 +169,66 @@ __global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict
   }
 }
 
+// ---- NpArray-order variants (contexts in MX_PREC_NPARRAY mode): the same
+// sequential fp32 loops as the CPU path, so results are bit-identical to it.
+
+// reduce_sum_to [rows, cols] -> [cols] (nparray/trait_impl.mbt:128-138):
+// one thread per column, rows ascending.
+__global__ void reduce_leading_seq_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                          int cols, int rows) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= cols) return;
+  float s = 0.0f;
+  for (int r = 0; r < rows; ++r) s = __fadd_rn(s, in[static_cast<int64_t>(r) * cols + col]);
+  out[col] = s;
+}
+
+// cross_entropy_with_labels + softmax_ce_backward_labels
+// (nparray/image_impl.mbt:83-114, 202-238): one thread per row, classes
+// ascending; row_loss[b] = -log p[label].
+__global__ void softmax_ce_seq_kernel(const float* __restrict__ logits,
+                                      const float* __restrict__ labels, float* __restrict__ grad,
+                                      float* __restrict__ row_loss, int batch, int C, float denom) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const float* row = logits + static_cast<int64_t>(b) * C;
+  const int label = static_cast<int>(labels[b]);
+  float mx_ = row[0];
+  for (int j = 1; j < C; ++j)
+    if (row[j] > mx_) mx_ = row[j];
+  float se = 0.0f;
+  for (int j = 0; j < C; ++j)
+    se = __fadd_rn(se, static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))));
+  const float lse = static_cast<float>(log(static_cast<double>(se)));
+  row_loss[b] = -__fsub_rn(__fsub_rn(row[label], mx_), lse);
+  if (grad) {
+    float* g = grad + static_cast<int64_t>(b) * C;
+    for (int j = 0; j < C; ++j) {
+      const float sm =
+          __fdiv_rn(static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))), se);
+      g[j] = __fdiv_rn(__fsub_rn(sm, j == label ? 1.0f : 0.0f), denom);
+    }
+  }
+}
+
+// One thread, elements ascending.  mode 0: out = (sum v) / denom;
+// mode 1: out = sqrt(sum v*v) (the optimizer's global norm,
+// nparray/trait_impl.mbt:288-295).
+__global__ void seq_sum_kernel(const float* __restrict__ v, int64_t n, float denom,
+                               float* __restrict__ out, int mode) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  float s = 0.0f;
+  if (mode == 0) {
+    for (int64_t i = 0; i < n; ++i) s = __fadd_rn(s, v[i]);
+    out[0] = __fdiv_rn(s, denom);
+  } else {
+    for (int64_t i = 0; i < n; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+    out[0] = __fsqrt_rn(s);
+  }
+}
+
+bool nparray_order(const Context* ctx) { return ctx->precision == MX_PREC_NPARRAY; }
+
 int grid_for(int64_t n, int num_sms, int per_sm = 8) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, num_sms * per_sm)));
 }
@@ -185,7 +246,10 @@ int relu_backward(Context* ctx, const float* g, const float* x, float* out, int6
 int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int rows,
                        cudaStream_t s) {
   if (cols <= 0) return kOk;
-  reduce_leading_kernel<<<(cols + 31) / 32, 256, 0, s>>>(in, out, cols, rows);
+  if (nparray_order(ctx))
+    reduce_leading_seq_kernel<<<(cols + 127) / 128, 128, 0, s>>>(in, out, cols, rows);
+  else
+    reduce_leading_kernel<<<(cols + 31) / 32, 256, 0, s>>>(in, out, cols, rows);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -193,6 +257,19 @@ int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int 
 int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
                       float* loss, int batch, int C, int denom, cudaStream_t s) {
   if (batch <= 0 || C <= 0) return kErrInvalid;
+  if (nparray_order(ctx)) {
+    int rc = ensure_small_scratch(ctx, static_cast<size_t>(batch) * sizeof(float));
+    if (rc != kOk) return rc;
+    float* row_loss = static_cast<float*>(ctx->small_scratch);
+    softmax_ce_seq_kernel<<<(batch + 127) / 128, 128, 0, s>>>(logits, labels, grad, row_loss,
+                                                              batch, C, static_cast<float>(denom));
+    note_launches(1);
+    if (loss) {
+      seq_sum_kernel<<<1, 1, 0, s>>>(row_loss, batch, static_cast<float>(denom), loss, 0);
+      note_launches(1);
+    }
+    return cuda_status(cudaGetLastError());
+  }
   const int blocks = (batch + 7) / 8;
   int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks) * sizeof(float));
   if (rc != kOk) return rc;
@@ -219,9 +296,14 @@ int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int6
   if (rc != kOk) return rc;
   float* partial = static_cast<float*>(ctx->small_scratch);
   float* norm = norm_out ? norm_out : partial + blocks;
-  norm_sq_kernel<<<blocks, 256, 0, s>>>(g, n, partial);
-  finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, 1.0f, norm, 1);
-  note_launches(3);  // norm_sq, finish_sum, sgd_update
+  if (nparray_order(ctx)) {
+    seq_sum_kernel<<<1, 1, 0, s>>>(g, n, 1.0f, norm, 1);
+    note_launches(2);  // seq_sum, sgd_update
+  } else {
+    norm_sq_kernel<<<blocks, 256, 0, s>>>(g, n, partial);
+    finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, 1.0f, norm, 1);
+    note_launches(3);  // norm_sq, finish_sum, sgd_update
+  }
   sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
                                                               max_norm, norm);
   return cuda_status(cudaGetLastError());

@@ -39,6 +39,9 @@ struct GemmArgs {
   float alpha = 1.0f, beta = 0.0f;
   const float* bias = nullptr;
   int relu = 0;
+  // NpArray order: fp32 multiply then add, k ascending, no split-K.  Only the
+  // SIMT kernel honours it; results are bit-identical to the CPU path.
+  int strict = 0;
 };
 
 // Grows ctx->workspace to at least `bytes` (stream-ordered free of the old

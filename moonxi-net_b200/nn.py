@@ -40,6 +40,57 @@ def _round_up(x: int, a: int = _ALIGN) -> int:
     return (x + a - 1) // a * a
 
 
+class FlatLayout:
+    """Offsets of the flat parameter / gradient / velocity buffers.
+
+    Parameters follow the reference's order [w1, b1, w2, b2, ...]
+    (MLP::params, moonxi-net/model/mlp.mbt:27-29); each block starts on a
+    256-byte boundary (zero padding between blocks).  The gradient buffer is
+    prefixed by a 64-float slot that carries the step's loss, so that the
+    loss rides in the first layer's all-reduce bucket.  Device-independent:
+    the data-parallel host logic is tested with it on CPU ranks.
+    """
+
+    def __init__(self, dims):
+        self.dims = list(dims)
+        self.L = len(dims) - 1
+        self.w_off, self.b_off = [], []
+        off = 0
+        for i in range(self.L):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            self.w_off.append(off)
+            off += _round_up(fi * fo)
+            self.b_off.append(off)
+            off += _round_up(fo)
+        self.n_flat = off
+        self.grads_buf_len = _LOSS_SLOTS + off
+
+    def w_range(self, i):
+        return self.w_off[i], self.w_off[i] + self.dims[i] * self.dims[i + 1]
+
+    def b_range(self, i):
+        return self.b_off[i], self.b_off[i] + self.dims[i + 1]
+
+    def bucket(self, i):
+        """[start, end) in the gradient buffer of layer i's all-reduce bucket
+        (its dW and db; bucket 0 also holds the loss slot)."""
+        start = self.w_off[i] + _LOSS_SLOTS if i > 0 else 0
+        end = _LOSS_SLOTS + (self.w_off[i + 1] if i + 1 < self.L else self.n_flat)
+        return start, end
+
+    def reduce_order(self):
+        """Buckets in the order backward produces them (last layer first)."""
+        return list(reversed(range(self.L)))
+
+
+def shard_rows(global_batch: int, rank: int, world: int):
+    """[begin, end) of this rank's rows of the global batch (equal shards)."""
+    if global_batch % world:
+        raise ValueError(f"global batch {global_batch} not divisible by {world} ranks")
+    per = global_batch // world
+    return rank * per, (rank + 1) * per
+
+
 class MLP:
     """A stack of Linear layers (ReLU between them) trained with momentum SGD.
 
@@ -58,7 +109,10 @@ class MLP:
         self.layout = layout
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
+        # The model's library context carries the precision mode, so the
+        # adjacent ops follow it too ("nparray": NpArray operation order).
         self.precision = precision
+        self.ctx = ops.context(self.device.index, precision)
         self.lr, self.momentum = float(lr), float(momentum)
         self.weight_decay, self.max_grad_norm = float(weight_decay), float(max_grad_norm)
         self.pg = process_group
@@ -68,21 +122,14 @@ class MLP:
         else:
             self.world = 1
 
-        # flat layout
-        self.w_off, self.b_off = [], []
-        off = 0
-        for i in range(self.L):
-            fi, fo = self.dims[i], self.dims[i + 1]
-            self.w_off.append(off)
-            off += _round_up(fi * fo)
-            self.b_off.append(off)
-            off += _round_up(fo)
-        self.n_flat = off
+        self.layout_ = FlatLayout(self.dims)
+        self.w_off, self.b_off = self.layout_.w_off, self.layout_.b_off
+        self.n_flat = self.layout_.n_flat
         dev = self.device
         self.params = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
         self.vels = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
         # grads_buf = [loss slot (64 floats)] + grads (n_flat)
-        self.grads_buf = torch.zeros(_LOSS_SLOTS + self.n_flat, device=dev, dtype=torch.float32)
+        self.grads_buf = torch.zeros(self.layout_.grads_buf_len, device=dev, dtype=torch.float32)
         self.grads = self.grads_buf[_LOSS_SLOTS:]
         self.loss_slot = self.grads_buf[:1]
         self.norm = torch.zeros(1, device=dev, dtype=torch.float32)
@@ -131,8 +178,7 @@ class MLP:
     def bucket(self, i):
         """Flat slice of grads_buf holding layer i's (dW, db); bucket 0 also
         carries the loss slot."""
-        start = self.w_off[i] + _LOSS_SLOTS if i > 0 else 0
-        end = _LOSS_SLOTS + (self.w_off[i + 1] if i + 1 < self.L else self.n_flat)
+        start, end = self.layout_.bucket(i)
         return self.grads_buf[start:end]
 
     def _buffers(self, B):
@@ -154,7 +200,7 @@ class MLP:
         for i in range(self.L):
             h = ops.linear(h, self.w[i], self.b[i], relu=(i + 1 < self.L),
                            transpose_w=(self.layout == "nt"), out=acts[i],
-                           precision=self.precision)
+                           ctx=self.ctx)
         return h
 
     def step(self, x: torch.Tensor, labels: torch.Tensor, global_batch: int | None = None,
@@ -165,7 +211,7 @@ class MLP:
         G = B * self.world if global_batch is None else int(global_batch)
         acts, gbuf = self._buffers(B)
         nt = self.layout == "nt"
-        prec = self.precision
+        ctx = self.ctx
         timer = self.gemm_timer
 
         def timed(flops, fn, *a, **k):
@@ -184,22 +230,22 @@ class MLP:
         for i in range(self.L):
             fi, fo = self.dims[i], self.dims[i + 1]
             timed(2 * B * fi * fo, ops.linear, h[i], self.w[i], self.b[i],
-                  relu=(i + 1 < self.L), transpose_w=nt, out=acts[i], precision=prec)
+                  relu=(i + 1 < self.L), transpose_w=nt, out=acts[i], ctx=ctx)
             h.append(acts[i])
         # loss and dlogits in one pass; the loss lands in the first bucket
         ops.softmax_ce_labels(h[self.L], labels, denom=G, grad=gbuf[self.L - 1],
-                              loss=self.loss_slot)
+                              loss=self.loss_slot, ctx=ctx)
         works = []
         g = gbuf[self.L - 1]
         for i in reversed(range(self.L)):
             fi, fo = self.dims[i], self.dims[i + 1]
-            ops.reduce_sum_leading(g, out=self.gb[i])
+            ops.reduce_sum_leading(g, out=self.gb[i], ctx=ctx)
             if nt:   # dW[out,in] = dY^T X
                 timed(2 * B * fi * fo, ops.matmul, g, h[i], fo, B, fi, ta=True, tb=False,
-                      out=self.gw[i], precision=prec)
+                      out=self.gw[i], ctx=ctx)
             else:    # dW[in,out] = X^T dY
                 timed(2 * B * fi * fo, ops.matmul, h[i], g, fi, B, fo, ta=True, tb=False,
-                      out=self.gw[i], precision=prec)
+                      out=self.gw[i], ctx=ctx)
             if self.pg is not None:
                 import torch.distributed as dist
                 works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
@@ -207,14 +253,15 @@ class MLP:
                 gprev = gbuf[i - 1]
                 # dX = dY W^T: w [in,out] -> stored [N=in, K=out] (tb=1); w [out,in] -> tb=0
                 timed(2 * B * fi * fo, ops.matmul, g, self.w[i], B, fo, fi, ta=False,
-                      tb=not nt, out=gprev, precision=prec)
-                ops.relu_backward(gprev, h[i], out=gprev)
+                      tb=not nt, out=gprev, ctx=ctx)
+                ops.relu_backward(gprev, h[i], out=gprev, ctx=ctx)
                 g = gprev
         for wk in works:
             wk.wait()
         if update:
             ops.sgd_momentum_autoclip(self.params, self.grads, self.vels, self.lr, self.momentum,
-                                      self.weight_decay, self.max_grad_norm, norm_out=self.norm)
+                                      self.weight_decay, self.max_grad_norm, norm_out=self.norm,
+                                      ctx=ctx)
         return self.loss_slot
 
     # ------------------------------------------------------------ CUDA graph

@@ -13,20 +13,29 @@ import torch
 from . import _lib
 from ._lib import PRECISIONS, check
 
-_ctx_cache: dict[int, int] = {}
+_ctx_cache: dict[tuple, int] = {}
 
 
-def context(device: int | None = None) -> int:
-    """The library context (the ABI's ``handle``) for a device, created once."""
+def context(device: int | None = None, mode: str = "default") -> int:
+    """The library context (the ABI's ``handle``) for a device and precision
+    mode, created once.  A context in "nparray" mode also runs the
+    training-step ops in the NpArray CPU order (bit-identical results)."""
     if device is None:
         device = torch.cuda.current_device()
-    h = _ctx_cache.get(device)
+    key = (int(device), mode)
+    h = _ctx_cache.get(key)
     if h is None:
-        h = _lib.lib().mx_context_create(device)
+        h = _lib.lib().mx_context_create(int(device))
         if not h:
             raise _lib.MXError(_lib.MX_ERR_NO_DEVICE, f"mx_context_create({device})")
-        _ctx_cache[device] = h
+        if mode != "default":
+            check(_lib.lib().mx_context_set_precision(h, _prec(mode)), "mx_context_set_precision")
+        _ctx_cache[key] = h
     return h
+
+
+def _handle(ctx, t: torch.Tensor) -> int:
+    return ctx if ctx is not None else context(t.device.index)
 
 
 def _prec(precision) -> int:
@@ -53,7 +62,8 @@ def _check_tensor(t: torch.Tensor, name: str, numel: int | None = None):
 
 def matmul(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = False,
            tb: bool = False, alpha: float = 1.0, beta: float = 0.0,
-           out: torch.Tensor | None = None, precision="default", stream=None) -> torch.Tensor:
+           out: torch.Tensor | None = None, precision="default", stream=None,
+           ctx=None) -> torch.Tensor:
     """C[M,N] = alpha op(A) op(B) + beta C (the reference's cuda_matmul)."""
     _check_tensor(a, "a", M * K)
     _check_tensor(b, "b", K * N)
@@ -61,7 +71,7 @@ def matmul(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = 
         out = torch.empty((M, N), device=a.device, dtype=torch.float32)
     _check_tensor(out, "out", M * N)
     rc = _lib.lib().moonbit_cuda_matmul_ex(
-        context(a.device.index), a.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, int(ta),
+        _handle(ctx, a), a.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, int(ta),
         int(tb), float(alpha), float(beta), _stream_ptr(stream), _prec(precision))
     check(rc, "moonbit_cuda_matmul_ex")
     return out
@@ -71,7 +81,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = Fa
          tb: bool = False, alpha: float = 1.0, beta: float = 0.0,
          bias: torch.Tensor | None = None, relu: bool = False,
          out: torch.Tensor | None = None, precision="default", stream=None,
-         lda: int = 0, ldb: int = 0, ldc: int = 0) -> torch.Tensor:
+         lda: int = 0, ldb: int = 0, ldc: int = 0, ctx=None) -> torch.Tensor:
     """C = act(alpha op(A) op(B) + beta C + bias) for any layout (mx_gemm_ex)."""
     _check_tensor(a, "a", M * K if not lda else 1)
     _check_tensor(b, "b", K * N if not ldb else 1)
@@ -81,7 +91,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = Fa
         out = torch.empty((M, N), device=a.device, dtype=torch.float32)
     _check_tensor(out, "out", M * N if not ldc else 1)
     rc = _lib.lib().mx_gemm_ex(
-        context(a.device.index), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+        _handle(ctx, a), a.data_ptr(), b.data_ptr(), out.data_ptr(),
         bias.data_ptr() if bias is not None else None, M, K, N, int(ta), int(tb), int(lda),
         int(ldb), int(ldc), float(alpha), float(beta), int(relu), _stream_ptr(stream),
         _prec(precision))
@@ -91,7 +101,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, M: int, K: int, N: int, ta: bool = Fa
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, relu: bool = False,
            transpose_w: bool = False, out: torch.Tensor | None = None, alpha: float = 1.0,
-           precision="default", stream=None) -> torch.Tensor:
+           precision="default", stream=None, ctx=None) -> torch.Tensor:
     """y = act(alpha x op(w) + bias): w is [K,N] (transpose_w=False) or [N,K]."""
     M, K = x.shape
     N = w.shape[0] if transpose_w else w.shape[1]
@@ -103,7 +113,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, relu: bo
         out = torch.empty((M, N), device=x.device, dtype=torch.float32)
     _check_tensor(out, "out", M * N)
     rc = _lib.lib().moonbit_cuda_linear_fwd_ex(
-        context(x.device.index), x.data_ptr(), w.data_ptr(),
+        _handle(ctx, x), x.data_ptr(), w.data_ptr(),
         bias.data_ptr() if bias is not None else None, out.data_ptr(), M, K, N,
         int(transpose_w), int(relu), float(alpha), _stream_ptr(stream), _prec(precision))
     check(rc, "moonbit_cuda_linear_fwd_ex")
@@ -111,13 +121,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, relu: bo
 
 
 def relu_backward(grad_out: torch.Tensor, saved: torch.Tensor, out: torch.Tensor | None = None,
-                  stream=None) -> torch.Tensor:
+                  stream=None, ctx=None) -> torch.Tensor:
     _check_tensor(grad_out, "grad_out")
     _check_tensor(saved, "saved", grad_out.numel())
     if out is None:
         out = torch.empty_like(grad_out)
     _check_tensor(out, "out", grad_out.numel())
-    rc = _lib.lib().mx_relu_backward(context(grad_out.device.index), grad_out.data_ptr(),
+    rc = _lib.lib().mx_relu_backward(_handle(ctx, grad_out), grad_out.data_ptr(),
                                      saved.data_ptr(), out.data_ptr(), grad_out.numel(),
                                      _stream_ptr(stream))
     check(rc, "mx_relu_backward")
@@ -125,14 +135,14 @@ def relu_backward(grad_out: torch.Tensor, saved: torch.Tensor, out: torch.Tensor
 
 
 def reduce_sum_leading(x: torch.Tensor, out: torch.Tensor | None = None,
-                       stream=None) -> torch.Tensor:
+                       stream=None, ctx=None) -> torch.Tensor:
     """Column sums of a [rows, cols] tensor (the bias gradient)."""
     rows, cols = x.shape
     _check_tensor(x, "x")
     if out is None:
         out = torch.empty((cols,), device=x.device, dtype=torch.float32)
     _check_tensor(out, "out", cols)
-    rc = _lib.lib().mx_reduce_sum_leading(context(x.device.index), x.data_ptr(), out.data_ptr(),
+    rc = _lib.lib().mx_reduce_sum_leading(_handle(ctx, x), x.data_ptr(), out.data_ptr(),
                                           cols, rows, _stream_ptr(stream))
     check(rc, "mx_reduce_sum_leading")
     return out
@@ -140,7 +150,7 @@ def reduce_sum_leading(x: torch.Tensor, out: torch.Tensor | None = None,
 
 def softmax_ce_labels(logits: torch.Tensor, labels: torch.Tensor, denom: int | None = None,
                       grad: torch.Tensor | None = None, loss: torch.Tensor | None = None,
-                      want_grad: bool = True, stream=None):
+                      want_grad: bool = True, stream=None, ctx=None):
     """(loss[1], dlogits) of mean cross-entropy with float class labels."""
     B, C = logits.shape
     _check_tensor(logits, "logits")
@@ -150,7 +160,7 @@ def softmax_ce_labels(logits: torch.Tensor, labels: torch.Tensor, denom: int | N
     if want_grad and grad is None:
         grad = torch.empty_like(logits)
     rc = _lib.lib().mx_softmax_ce_labels(
-        context(logits.device.index), logits.data_ptr(), labels.data_ptr(),
+        _handle(ctx, logits), logits.data_ptr(), labels.data_ptr(),
         grad.data_ptr() if want_grad else None, loss.data_ptr(), B, C,
         B if denom is None else int(denom), _stream_ptr(stream))
     check(rc, "mx_softmax_ce_labels")
@@ -160,12 +170,12 @@ def softmax_ce_labels(logits: torch.Tensor, labels: torch.Tensor, denom: int | N
 def sgd_momentum_autoclip(params: torch.Tensor, grads: torch.Tensor, vels: torch.Tensor, lr: float,
                           momentum: float, weight_decay: float, max_grad_norm: float,
                           norm_out: torch.Tensor | None = None, n: int | None = None,
-                          stream=None) -> None:
+                          stream=None, ctx=None) -> None:
     n = params.numel() if n is None else n
     for t, name in ((params, "params"), (grads, "grads"), (vels, "vels")):
         _check_tensor(t, name, n)
     rc = _lib.lib().mx_sgd_momentum_autoclip(
-        context(params.device.index), params.data_ptr(), grads.data_ptr(), vels.data_ptr(), n,
+        _handle(ctx, params), params.data_ptr(), grads.data_ptr(), vels.data_ptr(), n,
         float(lr), float(momentum), float(weight_decay), float(max_grad_norm),
         norm_out.data_ptr() if norm_out is not None else None, _stream_ptr(stream))
     check(rc, "mx_sgd_momentum_autoclip")

@@ -261,6 +261,53 @@ class MLPOracle:
         return loss
 
 
+class MLPFloat64:
+    """The same training step as MLPOracle evaluated in float64 with numpy
+    (no fp32 rounding anywhere).  Used to measure how far the fp32 oracle's
+    own loss curve drifts from exact arithmetic -- the conditioning floor for
+    any fp32 implementation that does not reproduce NpArray's operation order."""
+
+    def __init__(self, weights, biases, lr=0.01, momentum=0.9, weight_decay=1e-4,
+                 max_grad_norm=35.0):
+        self.w = [np.asarray(w, np.float64).copy() for w in weights]   # [in, out]
+        self.b = [np.asarray(b, np.float64).copy() for b in biases]
+        self.vw = [np.zeros_like(w) for w in self.w]
+        self.vb = [np.zeros_like(b) for b in self.b]
+        self.lr, self.m, self.wd, self.max_norm = lr, momentum, weight_decay, max_grad_norm
+
+    def step(self, x, labels):
+        B = x.shape[0]
+        lab = np.asarray(labels).astype(np.int64)
+        h, pre = [np.asarray(x, np.float64)], []
+        L = len(self.w)
+        for i in range(L):
+            a = h[-1] @ self.w[i] + self.b[i]
+            pre.append(a)
+            h.append(np.maximum(a, 0.0) if i + 1 < L else a)
+        z = h[-1]
+        mx = z.max(1, keepdims=True)
+        e = np.exp(z - mx)
+        s = e.sum(1, keepdims=True)
+        loss = float(np.mean(np.log(s[:, 0]) + mx[:, 0] - z[np.arange(B), lab]))
+        g = e / s
+        g[np.arange(B), lab] -= 1.0
+        g /= B
+        gw, gb = [None] * L, [None] * L
+        for i in reversed(range(L)):
+            gb[i] = g.sum(0)
+            gw[i] = h[i].T @ g
+            if i > 0:
+                g = (g @ self.w[i].T) * (pre[i - 1] > 0)
+        norm = np.sqrt(sum(float((q * q).sum()) for q in gw + gb))
+        clip = self.max_norm / norm if norm > self.max_norm else 1.0
+        for i in range(L):
+            self.vw[i] = self.m * self.vw[i] + gw[i] * clip + self.wd * self.w[i]
+            self.w[i] = self.w[i] - self.lr * self.vw[i]
+            self.vb[i] = self.m * self.vb[i] + gb[i] * clip + self.wd * self.b[i]
+            self.b[i] = self.b[i] - self.lr * self.vb[i]
+        return loss
+
+
 # --------------------------------------------------------------------------
 # fp64 helpers for error bounds
 # --------------------------------------------------------------------------

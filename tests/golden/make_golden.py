@@ -111,16 +111,23 @@ def write_mlp784_step():
 def write_loss_curve(steps=200):
     w, b, x, y = synthetic.mlp_problem("mlp3072")
     m = oracle.MLPOracle(w, b, layout="nn", threads=oracle.default_threads())
-    losses = []
+    m64 = oracle.MLPFloat64(w, b)
+    losses, l64 = [], []
     for s in range(steps):
         losses.append(m.step(x, y))
+        l64.append(m64.step(x, y))
         if s % 20 == 0:
-            print(f"step {s}: loss {losses[-1]:.6f}", flush=True)
+            print(f"step {s}: loss {losses[-1]:.6f} fp64 {l64[-1]:.6f}", flush=True)
+    dev = [abs(float(a) - b) for a, b in zip(losses, l64)]
     out = {
         "config": "mlp3072 batch 512 seed 2, layout nn, same batch each step, "
                   "momentum SGD lr 0.01 m 0.9 wd 1e-4 clip 35",
         "steps": steps,
         "loss_hex": [f32hex(v) for v in losses],
+        # the same run in float64 (oracle.MLPFloat64): how far exact arithmetic
+        # lands from the fp32 NpArray curve
+        "loss_fp64": [repr(v) for v in l64],
+        "max_abs_dev_fp64_vs_oracle": max(dev),
     }
     with open(os.path.join(HERE, "mlp3072_loss_curve.json"), "w") as f:
         json.dump(out, f, indent=0)

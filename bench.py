@@ -374,6 +374,39 @@ def run_ours(args):
     return 0
 
 
+def run_gemm_only(args):
+    """One square GEMM, K timed launches after W warm-ups (L2 flushed between
+    launches); the small case the kernel profiles are taken on."""
+    import torch
+
+    from moonxi_net_b200 import ops
+    torch.cuda.set_device(0)
+    n = args.gemm
+    ta, tb = {"nn": (0, 0), "nt": (0, 1), "tn": (1, 0)}[args.layout]
+    a = torch.randn((n, n), device="cuda")
+    b = torch.randn((n, n), device="cuda")
+    c = torch.empty((n, n), device="cuda")
+    flush = torch.empty(int(256e6) // 4, device="cuda")
+    prec = "3xtf32" if args.precision == "auto" else args.precision
+    for _ in range(args.warmup):
+        ops.gemm(a, b, n, n, n, ta=ta, tb=tb, out=c, precision=prec)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.gemm(a, b, n, n, n, ta=ta, tb=tb, out=c, precision=prec)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.median(times)
+    print(json.dumps({"metric": f"GEMM {n}^3 {args.layout} TFLOP/s", "precision": prec,
+                      "value": 2.0 * n ** 3 / t / 1e12, "unit": "TFLOP/s", "ms": t * 1e3,
+                      "steps": args.steps, "warmup": args.warmup}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -385,10 +418,15 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--gemm", type=int, default=0, metavar="N",
+                    help="time only the square N^3 GEMM of --precision (profiling case)")
+    ap.add_argument("--layout", default="nn", choices=["nn", "nt", "tn"])
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps
     if args.impl == "reference":
         return run_reference(args)
+    if args.gemm:
+        return run_gemm_only(args)
     return run_ours(args)
 
 

@@ -101,6 +101,34 @@ int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float* c, const
                    int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, int32_t relu,
                    void* stream, int32_t precision);
 
+/* Allocation-free 3xTF32 GEMM.  No counterpart in the reference: it exists
+ * for callers that must not allocate device memory inside a library call --
+ * for example a host runtime that reserved its whole device-memory budget up
+ * front and hands out slices itself (as the reference GPU backend does with
+ * its single bump pool), or a process running under a fixed memory budget.
+ * Same math and arguments as mx_gemm_ex with transpose flags, packed leading
+ * dimensions (cuda_matmul's) and MX_PREC_3XTF32, on the current device and
+ * the given stream (NULL = legacy default stream).  It calls no cudaMalloc or
+ * cudaFree and no allocating library routine: its scratch (the hi/lo split
+ * copies of A and B) is a 64 MiB array compiled into this library, which
+ * every GPU that loads the library holds until the process exits.
+ *   - Limit: the split copies need 2 * (M*Kp + N*Kp) * 4 bytes (Kp = K
+ *     rounded up to a multiple of 4, each copy padded to 256 bytes), at most
+ *     64 MiB; larger problems are rejected with MX_ERR_UNSUPPORTED before
+ *     anything is launched.
+ *   - The first call on a device looks up the device address of that array
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call, on every stream, shares the one array, which keeps the last
+ *     call's contents: calls that overlap on the GPU race and corrupt each
+ *     other's results.  Serialise them (one stream, or events).
+ *   - dev_status: optional device pointer to two int32 words; a bounded
+ *     in-kernel wait that gives up writes MX_ERR_TIMEOUT and the call site
+ *     there (NULL: into a status word inside the library). */
+int32_t mx_gemm_3xtf32_noalloc(const float* a, const float* b, float* c, const float* bias,
+                               int32_t M, int32_t K, int32_t N, int32_t transpose_a,
+                               int32_t transpose_b, float alpha, float beta, int32_t relu,
+                               int32_t* dev_status, void* stream);
+
 /* cudaSetDevice for the calling host thread (the reference hard-codes
  * device 0 at every call site, moonxi-net-gpu/cuda/gpu_context.mbt:57-83). */
 int32_t moonbit_cuda_set_device(int32_t device);

@@ -26,6 +26,7 @@
 // abort flag, records kErrTimeout, drains in-flight copies and MMAs, frees
 // TMEM and returns.
 #include <algorithm>
+#include <mutex>
 
 #include "mx_internal.h"
 #include "mx_ptx.cuh"
@@ -426,3 +427,129 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
 }
 
 }  // namespace mx
+
+// ===========================================================================
+// Allocation-free entry point: mx_gemm_3xtf32_noalloc.
+//
+// Some callers may not allocate device memory at all: a host runtime that
+// reserved its whole device-memory budget up front and hands out slices of
+// it itself (the reference GPU backend does this with one cudaMalloc'd bump
+// pool, moonxi-net-gpu/cuda/cuda_kernels.cu:922-1004), or a process that
+// runs under a fixed memory budget where a hidden cudaMalloc inside a library
+// call could fail or evict someone else.  The regular entry points grow a
+// per-context workspace with cudaMalloc the first time a large shape needs
+// it; this one never does.  Its scratch (the hi/lo split copies of A and B)
+// lives in a fixed-size array compiled into this library, which every GPU
+// that loads the library holds until the process exits.
+// ===========================================================================
+namespace mx {
+namespace {
+
+// Upper bound of the split-operand scratch: 64 MiB, i.e. roughly
+// (M + N) * K <= 8 Mi elements (2048^3 fits; the exact check is below).
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+__device__ __align__(256) int g_noalloc_status[2];
+
+struct NoAllocDevice {
+  bool ready = false;
+  uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch
+  int* status = nullptr;       // device address of g_noalloc_status
+  int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+// Once per device, with that device current: resolve the device addresses of
+// the static arrays.  In host code the array names are host-side stand-ins,
+// not device addresses, so kernels only ever receive these resolved pointers.
+int noalloc_setup(NoAllocDevice** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64) return kErrUnsupported;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    d.scratch = static_cast<uint8_t*>(p);
+    e = cudaGetSymbolAddress(&p, g_noalloc_status);
+    if (e != cudaSuccess) return cuda_status(e);
+    d.status = static_cast<int*>(p);
+    e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    d.ready = true;
+  }
+  *out = &d;
+  return kOk;
+}
+
+}  // namespace
+}  // namespace mx
+
+extern "C" __attribute__((visibility("default"))) int32_t mx_gemm_3xtf32_noalloc(
+    const float* a, const float* b, float* c, const float* bias, int32_t M, int32_t K,
+    int32_t N, int32_t transpose_a, int32_t transpose_b, float alpha, float beta, int32_t relu,
+    int32_t* dev_status, void* stream) {
+  using namespace mx;
+  if (M < 0 || N < 0 || K < 0) return kErrInvalid;
+  if (M == 0 || N == 0) return kOk;
+  if (!c || ((!a || !b) && K > 0)) return kErrInvalid;
+  GemmArgs g;
+  g.a = a; g.b = b; g.c = c;
+  g.M = M; g.K = K; g.N = N;
+  g.ta = transpose_a ? 1 : 0; g.tb = transpose_b ? 1 : 0;
+  g.lda = g.ta ? M : K;   // packed leading dimensions, as cuda_matmul
+  g.ldb = g.tb ? K : N;
+  g.ldc = N;
+  g.alpha = alpha; g.beta = beta; g.bias = bias; g.relu = relu ? 1 : 0;
+  const size_t need = tc_gemm_workspace_bytes(g, 3);
+  if (need > kNoAllocScratchBytes) return kErrUnsupported;  // beyond the static scratch
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_setup(&d);
+  if (rc != kOk) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = dev_status ? reinterpret_cast<int*>(dev_status) : d->status;
+
+  if (K == 0) {  // no product: the SIMT epilogue computes beta*C + bias, no scratch
+    Context local;
+    local.num_sms = d->num_sms;
+    local.status = status;
+    return simt_gemm_launch(&local, g, s, nullptr, 0);
+  }
+  const int64_t Kp = (static_cast<int64_t>(K) + 3) & ~static_cast<int64_t>(3);
+  uint8_t* ws = d->scratch;  // same carve-up as the workspace of tc_gemm
+  float* a_hi = reinterpret_cast<float*>(ws);
+  ws += align256(static_cast<size_t>(M) * Kp * 4);
+  float* b_hi = reinterpret_cast<float*>(ws);
+  ws += align256(static_cast<size_t>(N) * Kp * 4);
+  float* a_lo = reinterpret_cast<float*>(ws);
+  ws += align256(static_cast<size_t>(M) * Kp * 4);
+  float* b_lo = reinterpret_cast<float*>(ws);
+  // The split kernels overwrite every scratch element the main kernel reads
+  // (columns [K, Kp) are outside the tensor maps), so nothing needs clearing.
+  cudaError_t e = launch_split(a, g.lda, g.ta == 0, M, K, Kp, a_hi, a_lo, d->num_sms, s);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = launch_split(b, g.ldb, g.tb != 0, N, K, Kp, b_hi, b_lo, d->num_sms, s);
+  if (e != cudaSuccess) return cuda_status(e);
+  CUtensorMap tah{}, tal{}, tbh{}, tbl{};
+  const bool ok =
+      make_tmap_2d(&tah, a_hi, K, M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_tmap_2d(&tbh, b_hi, K, N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_tmap_2d(&tal, a_lo, K, M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_tmap_2d(&tbl, b_lo, K, N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok) return kErrUnsupported;
+  TcParams p{};
+  p.c = c; p.bias = bias; p.status = status; p.ldc = g.ldc;
+  p.M = M; p.N = N; p.K = K;
+  p.tiles_m = (M + kBM - 1) / kBM;
+  p.tiles_n = (N + kBN - 1) / kBN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.alpha = alpha; p.beta = beta; p.relu = g.relu;
+  p.timeout_ns = 2000000000ull;
+  e = launch_tc<3>(tah, tal, tbh, tbl, p, std::min(p.num_tiles, d->num_sms), s);
+  return e == cudaSuccess ? kOk : cuda_status(e);
+}

@@ -1,0 +1,98 @@
+"""Data-parallel training step on 2 GPUs (NCCL), against one GPU.
+
+Each rank runs the MLP step on its half of the batch with the loss scaled by
+1/global_batch and all-reduces the per-layer gradient buckets; both replicas
+must end bit-identical, and match a single-GPU run on the whole batch within
+the fp32-class tolerance.  The step is also captured in a CUDA graph with its
+all-reduces and replayed.  Needs two visible GPUs (skipped otherwise).
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+pytestmark = pytest.mark.gpu
+STEPS = 3
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir, use_graph):
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+    from moonxi_net_b200 import nn, synthetic
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        w, b, x, y = synthetic.mlp_problem("mlp3072", batch=512)
+        lo, hi = nn.shard_rows(512, rank, world)
+        X = torch.from_numpy(x[lo:hi].copy()).to(dev)
+        Y = torch.from_numpy(y[lo:hi].copy()).to(dev)
+        m = nn.MLP([3072, 1024, 1024, 10], w, b, precision="3xtf32",
+                   process_group=dist.group.WORLD)
+        losses = []
+        if use_graph:
+            losses.append(float(m.step(X, Y, 512).item()))
+            m.capture(X, Y, 512)
+            for _ in range(STEPS - 1):
+                losses.append(float(m.replay().item()))
+            m.release_graph()
+        else:
+            for _ in range(STEPS):
+                losses.append(float(m.step(X, Y, 512).item()))
+        torch.cuda.synchronize()
+        np.savez(os.path.join(outdir, f"rank{rank}.npz"), params=m.params.cpu().numpy(),
+                 losses=np.array(losses))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(use_graph):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.get_context("spawn")
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, use_graph)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+            if p.is_alive():
+                p.kill()
+                pytest.fail("a rank did not finish")
+        assert [p.exitcode for p in procs] == [0, 0]
+        return [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_dp2_matches_single_gpu(cuda_device, use_graph):
+    from moonxi_net_b200 import nn, synthetic
+    r0, r1 = _run(use_graph)
+    assert np.array_equal(r0["params"], r1["params"])       # identical replicas
+    assert np.array_equal(r0["losses"], r1["losses"])
+    w, b, x, y = synthetic.mlp_problem("mlp3072", batch=512)
+    m = nn.MLP([3072, 1024, 1024, 10], w, b, precision="3xtf32")
+    X, Y = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    losses = [float(m.step(X, Y).item()) for _ in range(STEPS)]
+    ref = m.params.cpu().numpy().astype(np.float64)
+    got = r0["params"].astype(np.float64)
+    assert np.linalg.norm(got - ref) <= 1e-5 * np.linalg.norm(ref)
+    assert np.allclose(r0["losses"], losses, rtol=0, atol=1e-5)

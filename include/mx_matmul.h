@@ -101,6 +101,31 @@ int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float* c, const
                    int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, int32_t relu,
                    void* stream, int32_t precision);
 
+/* ---- Split-form (3xTF32) operands, produced once by the kernels that write
+ * them instead of by a prepass inside every matmul.  A split copy of x is
+ * hi = tf32_rna(x), lo = tf32_rna(x - hi), stored as fp32 bit patterns. */
+
+/* hi/lo split of a row-major [rows, cols] matrix (leading dimension ld) into
+ * hi/lo with leading dimension ld_out (lo may be NULL: TF32 only).  New; the
+ * reference has no split operands. */
+int32_t mx_split_tf32(void* handle, const float* src, int32_t rows, int32_t cols, int64_t ld,
+                      float* hi, float* lo, int64_t ld_out, void* stream);
+
+/* The tcgen05 GEMM on split operands: C[M,N] = act(alpha A B + beta C +
+ * bias), optionally zeroed where mask[row*ldm+col] <= 0 (the ReLU backward of
+ * the layer below, grad/image.mbt:45-61), written to c and/or as a split copy
+ * to c_hi/c_lo (leading dimension ldc).  a_kmajor = 1: A(m,k) at
+ * a[m*lda + k]; 0: at a[k*lda + m] (B likewise with n).  passes = 3: 3xTF32
+ * (a_lo/b_lo used), 1: TF32.  Base pointers and leading dimensions must be
+ * 16-byte multiples (TMA); M, N, K >= 1.  Used by the Linear/MLP step for
+ * X W, dY W^T and X^T dY (grad/blas.mbt:35,37) without any transpose. */
+int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo, int64_t lda,
+                         int32_t a_kmajor, const float* b_hi, const float* b_lo, int64_t ldb,
+                         int32_t b_kmajor, float* c, float* c_hi, float* c_lo, int64_t ldc,
+                         int32_t M, int32_t K, int32_t N, float alpha, float beta,
+                         const float* bias, int32_t relu, const float* mask, int64_t ldm,
+                         int32_t passes, void* stream);
+
 /* Allocation-free 3xTF32 GEMM.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory inside a library call --
  * for example a host runtime that reserved its whole device-memory budget up
@@ -202,6 +227,20 @@ int32_t mx_softmax_ce_labels(void* handle, const float* logits, const float* lab
 int32_t mx_sgd_momentum_autoclip(void* handle, float* params, const float* grads, float* vels,
                                  int64_t n, float lr, float momentum, float weight_decay,
                                  float max_grad_norm, float* norm_out, void* stream);
+
+/* mx_softmax_ce_labels that also writes the split copy g_hi/g_lo of the
+ * gradient (same layout) for the split-form backward GEMMs. */
+int32_t mx_softmax_ce_labels_split(void* handle, const float* logits, const float* labels,
+                                   float* grad, float* g_hi, float* g_lo, float* loss,
+                                   int32_t batch, int32_t num_classes, int32_t denom,
+                                   void* stream);
+
+/* mx_sgd_momentum_autoclip that also writes the split copy p_hi/p_lo of the
+ * updated parameters (same flat layout) for the next step's GEMMs. */
+int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, const float* grads,
+                                       float* vels, int64_t n, float lr, float momentum,
+                                       float weight_decay, float max_grad_norm, float* norm_out,
+                                       float* p_hi, float* p_lo, void* stream);
 
 #ifdef __cplusplus
 }

@@ -51,7 +51,15 @@ SIGNATURES = {
                                           _i32, _f32, _vp, _i32]),
     "mx_gemm_ex": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _i64,
                           _i64, _f32, _f32, _i32, _vp, _i32]),
-    "mx_gemm_3xtf32_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,
+    "mx_split_tf32": (_i32, [_vp, _vp, _i32, _i32, _i64, _vp, _vp, _i64, _vp]),
+    "mx_gemm_split_ex": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i32, _vp, _vp, _vp,
+                                _i64, _i32, _i32, _i32, _f32, _f32, _vp, _i32, _vp, _i64, _i32,
+                                _vp]),
+    "mx_softmax_ce_labels_split": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                          _vp]),
+    "mx_sgd_momentum_autoclip_split": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32,
+                                              _vp, _vp, _vp, _vp]),
+    "mx_gemm_3xtf32_noalloc":(_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,
                                       _f32, _i32, _vp, _vp]),
     "moonbit_cuda_set_device": (_i32, [_i32]),
     "mx_context_create": (_vp, [_i32]),

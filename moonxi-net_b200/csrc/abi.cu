@@ -184,7 +184,7 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
   if (row_stride_bytes % 16 != 0 || (box_inner * 4) % 16 != 0) return false;
   if (box_inner > 256 || box_outer > 256 || inner == 0 || outer == 0) return false;
-  if (swizzle == CU_TENSOR_MAP_SWIZZLE_128B && box_inner * 4 > 128) return false;
+  if (swizzle >= CU_TENSOR_MAP_SWIZZLE_128B && box_inner * 4 > 128) return false;
   if (swizzle == CU_TENSOR_MAP_SWIZZLE_64B && box_inner * 4 > 64) return false;
   if (inner >= (1ull << 32) || outer >= (1ull << 32)) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -193,6 +193,27 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3],
+                  const uint64_t strides_bytes[2], const uint32_t box[3],
+                  CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if (strides_bytes[0] % 16 != 0 || strides_bytes[1] % 16 != 0 || (box[0] * 4) % 16 != 0)
+    return false;
+  for (int i = 0; i < 3; ++i)
+    if (box[i] == 0 || box[i] > 256 || dims[i] == 0 || dims[i] >= (1ull << 32)) return false;
+  if (swizzle >= CU_TENSOR_MAP_SWIZZLE_128B && box[0] * 4 > 128) return false;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), d, st, b,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -303,6 +324,38 @@ MX_EXPORT int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float
   g.bias = bias;
   g.relu = relu ? 1 : 0;
   return run_gemm(ctx, g, precision, pick_stream(ctx, stream));
+}
+
+MX_EXPORT int32_t mx_split_tf32(void* handle, const float* src, int32_t rows, int32_t cols,
+                                int64_t ld, float* hi, float* lo, int64_t ld_out, void* stream) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  if (rows < 0 || cols < 0 || ld < cols || ld_out < cols) return MX_ERR_INVALID;
+  if (rows > 0 && cols > 0 && (!src || !hi)) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(ctx, stream);
+  return finish(ctx, split_tf32(ctx, src, ld, rows, cols, hi, lo, ld_out, s), s);
+}
+
+MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo,
+                                   int64_t lda, int32_t a_kmajor, const float* b_hi,
+                                   const float* b_lo, int64_t ldb, int32_t b_kmajor, float* c,
+                                   float* c_hi, float* c_lo, int64_t ldc, int32_t M, int32_t K,
+                                   int32_t N, float alpha, float beta, const float* bias,
+                                   int32_t relu, const float* mask, int64_t ldm, int32_t passes,
+                                   void* stream) {
+  Context* ctx = resolve(handle);
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  if (M < 0 || N < 0 || K < 1) return MX_ERR_INVALID;
+  if (lda < (a_kmajor ? K : M) || ldb < (b_kmajor ? K : N) || ldc < N) return MX_ERR_INVALID;
+  if (mask && ldm < N) return MX_ERR_INVALID;
+  if (!c_hi && c_lo) return MX_ERR_INVALID;
+  TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  SplitOperand A{a_hi, a_lo, lda, a_kmajor != 0}, B{b_hi, b_lo, ldb, b_kmajor != 0};
+  TcEpilogue E;
+  E.c = c; E.ldc = ldc; E.alpha = alpha; E.beta = beta; E.bias = bias; E.relu = relu ? 1 : 0;
+  E.mask = mask; E.ldm = ldm; E.c_hi = c_hi; E.c_lo = c_lo;
+  cudaStream_t s = pick_stream(ctx, stream);
+  return finish(ctx, tc_gemm_split(L, A, B, E, M, N, K, passes, s), s);
 }
 
 MX_EXPORT int32_t moonbit_cuda_set_device(int32_t device) {
@@ -446,6 +499,37 @@ MX_EXPORT int32_t mx_softmax_ce_labels(void* handle, const float* logits, const 
   if (!logits || !labels || batch <= 0 || num_classes <= 0 || denom <= 0) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
   return finish(c, softmax_ce_labels(c, logits, labels, grad, loss, batch, num_classes, denom, s),
+                s);
+}
+
+MX_EXPORT int32_t mx_softmax_ce_labels_split(void* handle, const float* logits,
+                                             const float* labels, float* grad, float* g_hi,
+                                             float* g_lo, float* loss, int32_t batch,
+                                             int32_t num_classes, int32_t denom, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (!logits || !labels || !grad || !g_hi || !g_lo || batch <= 0 || num_classes <= 0 ||
+      denom <= 0)
+    return MX_ERR_INVALID;
+  if (c->precision == MX_PREC_NPARRAY) return MX_ERR_UNSUPPORTED;  // split form is the fast path
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c, softmax_ce_labels(c, logits, labels, grad, loss, batch, num_classes, denom, s,
+                                     g_hi, g_lo),
+                s);
+}
+
+MX_EXPORT int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, const float* grads,
+                                                 float* vels, int64_t n, float lr,
+                                                 float momentum, float weight_decay,
+                                                 float max_grad_norm, float* norm_out,
+                                                 float* p_hi, float* p_lo, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (n < 0 || (n > 0 && (!params || !grads || !vels || !p_hi || !p_lo))) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c,
+                sgd_momentum_autoclip(c, params, grads, vels, n, lr, momentum, weight_decay,
+                                      max_grad_norm, norm_out, s, p_hi, p_lo),
                 s);
 }
 

@@ -34,13 +34,21 @@
 namespace mx {
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 16;  // kBK fp32 = 64-byte rows
+constexpr int kBM = 128, kBN = 256, kBK = 16;  // kBK fp32 = 64-byte K-major rows
 constexpr int kATile = kBM * kBK * 4;           // 8 KB
 constexpr int kBTile = kBN * kBK * 4;           // 16 KB
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
-constexpr uint32_t kSbo = 8 * kBK * 4;          // 8 rows x 64 B = 512 B
-constexpr uint32_t kLayoutSw64 = 4;
+// K-major tile: [rows][16] fp32, 64-byte rows, 64-byte swizzle; 8-row groups
+// 512 B apart.  MN-major tile: 32-wide MN chunks of [16 k][32 mn], 128-byte
+// rows; tf32 MN-major operands need the 128-byte swizzle with 32-byte atoms
+// (TMA SWIZZLE_128B_ATOM_32B, UMMA layout 128B_BASE32B): 4-row K groups
+// 512 B apart, chunks 2048 B apart, an 8-deep MMA slice = 8 rows = 1024 B.
+constexpr uint32_t kSboK = 8 * kBK * 4;         // 512 B
+constexpr uint32_t kSboMN = 4 * 128;            // 512 B
+constexpr uint32_t kK8MN = 8 * 128;             // 1024 B
+constexpr uint32_t kChunkMN = kBK * 128;        // 2048 B
+constexpr uint32_t kLayoutSw64 = 4, kLayoutSw128Base32 = 1;
 
 template <int PASSES>
 struct Cfg {
@@ -51,15 +59,19 @@ struct Cfg {
 };
 
 struct TcParams {
-  float* c;
+  float* c;             // may be null when only the split output is wanted
   const float* bias;
+  const float* mask;    // ReLU-backward mask: output zeroed where mask <= 0
+  float* c_hi;          // optional hi/lo split of the output (same ldc)
+  float* c_lo;
   int* status;
-  int64_t ldc;
+  int64_t ldc, ldm;
   int M, N, K;
   int tiles_m, tiles_n, num_tiles;
   float alpha, beta;
   int relu;
   uint64_t timeout_ns;
+  bool a_map3d, b_map3d;  // MN-major operand loaded by one 3-D copy per tile
 };
 
 // Grouped raster: bands of 16 M-tiles, N-major inside a band, so the CTAs
@@ -74,7 +86,31 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gm;
 }
 
-template <int PASSES>
+// One operand tile (rows x 16 k) of one copy (hi or lo) into shared memory.
+// MN-major tiles are 32-wide chunks: one 3-D copy (32 mn x 16 k x chunks)
+// when the operand's row count is a multiple of 32 (map3d), else one 2-D
+// copy per chunk (out-of-range rows then read as zeros).
+template <bool KMAJOR, int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                             int k0, int r0, bool map3d) {
+  if (KMAJOR) {
+    tma_load_2d(dst, map, bar, k0, r0);
+  } else if (map3d) {
+    tma_load_3d(dst, map, bar, 0, k0, r0 / 32);
+  } else {
+#pragma unroll
+    for (int c = 0; c < ROWS / 32; ++c) tma_load_2d(dst + c * kChunkMN, map, bar, r0 + 32 * c, k0);
+  }
+}
+
+// Descriptor of the k8-th 8-deep slice of an operand tile.
+template <bool KMAJOR>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int k8) {
+  if (KMAJOR) return sdesc_kmajor(saddr + k8 * 32, kSboK, kLayoutSw64);
+  return sdesc_mnmajor(saddr + k8 * kK8MN, kChunkMN, kSboMN, kLayoutSw128Base32);
+}
+
+template <int PASSES, bool AK, bool BKM>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
@@ -144,13 +180,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           armed[stage] = true;
           armed_parity[stage] = phase;
           const int k0 = kb * kBK;
-          tma_load_2d(base, &tmAh, &full[stage], k0, tm * kBM);
+          load_operand<AK, kBM>(base, &tmAh, &full[stage], k0, tm * kBM, p.a_map3d);
           if (PASSES == 3) {
-            tma_load_2d(base + kATile, &tmAl, &full[stage], k0, tm * kBM);
-            tma_load_2d(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN);
-            tma_load_2d(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0, tn * kBN);
+            load_operand<AK, kBM>(base + kATile, &tmAl, &full[stage], k0, tm * kBM, p.a_map3d);
+            load_operand<BKM, kBN>(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN,
+                                   p.b_map3d);
+            load_operand<BKM, kBN>(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0, tn * kBN,
+                                   p.b_map3d);
           } else {
-            tma_load_2d(base + kATile, &tmBh, &full[stage], k0, tn * kBN);
+            load_operand<BKM, kBN>(base + kATile, &tmBh, &full[stage], k0, tn * kBN, p.b_map3d);
           }
           if (++stage == C::kStages) {
             stage = 0;
@@ -169,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(kBM, kBN);
+      const uint32_t idesc = idesc_tf32(kBM, kBN, !AK, !BKM);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -197,12 +235,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t s_bl = s_base + 2 * kATile + kBTile;
 #pragma unroll
           for (int k8 = 0; k8 < kBK / 8; ++k8) {
-            const uint32_t koff = k8 * 32;  // 8 tf32 = 32 bytes along the swizzled row
-            const uint64_t ah = sdesc_kmajor(s_ah + koff, kSbo, kLayoutSw64);
-            const uint64_t bh = sdesc_kmajor(s_bh + koff, kSbo, kLayoutSw64);
+            const uint64_t ah = operand_desc<AK>(s_ah, k8);
+            const uint64_t bh = operand_desc<BKM>(s_bh, k8);
             if (PASSES == 3) {
-              const uint64_t al = sdesc_kmajor(s_al + koff, kSbo, kLayoutSw64);
-              const uint64_t bl = sdesc_kmajor(s_bl + koff, kSbo, kLayoutSw64);
+              const uint64_t al = operand_desc<AK>(s_al, k8);
+              const uint64_t bl = operand_desc<BKM>(s_bl, k8);
               mma_tf32(d_tmem, al, bh, idesc, accumulate);
               mma_tf32(d_tmem, ah, bl, idesc, 1u);
               mma_tf32(d_tmem, ah, bh, idesc, 1u);
@@ -231,7 +268,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int lane_grp = warp & 3;                 // TMEM lanes this warp may access
     const int row_in_tile = lane_grp * 32 + lane;
-    const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0);
+    const bool vec_ok =
+        (p.ldc % 4 == 0) &&
+        ((reinterpret_cast<uintptr_t>(p.c) | reinterpret_cast<uintptr_t>(p.c_hi) |
+          reinterpret_cast<uintptr_t>(p.c_lo)) & 15u) == 0;
+    const bool mask_vec = (p.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0);
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -241,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int row = tm * kBM + row_in_tile;
-      float* crow = p.c + static_cast<int64_t>(row) * p.ldc;
+      const int64_t roff = static_cast<int64_t>(row) * p.ldc;
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         uint32_t r[32];
@@ -252,27 +293,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         const int col0 = tn * kBN + chunk * 32;
         if (row < p.M && col0 < p.N) {
-        float v[32];
+          const bool full_chunk = col0 + 32 <= p.N;
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = p.alpha * __uint_as_float(r[j]);
-          const int col = col0 + j;
-          if (col < p.N) {
-            if (p.beta != 0.0f) x = x + p.beta * crow[col];
-            if (p.bias) x = x + __ldg(p.bias + col);
-            if (p.relu) x = x > 0.0f ? x : 0.0f;
+          for (int j = 0; j < 32; ++j) {
+            float x = p.alpha * __uint_as_float(r[j]);
+            const int col = col0 + j;
+            if (col < p.N) {
+              if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col];
+              if (p.bias) x = x + __ldg(p.bias + col);
+              if (p.relu) x = x > 0.0f ? x : 0.0f;
+            }
+            v[j] = x;
           }
-          v[j] = x;
-        }
-        if (vec_ok && col0 + 32 <= p.N) {
+          if (p.mask) {
+            const float* mrow = p.mask + static_cast<int64_t>(row) * p.ldm + col0;
+            if (mask_vec && full_chunk) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
+              for (int j = 0; j < 32; j += 4) {
+                const float4 m4 = __ldg(reinterpret_cast<const float4*>(mrow + j));
+                v[j] = m4.x > 0.0f ? v[j] : 0.0f;
+                v[j + 1] = m4.y > 0.0f ? v[j + 1] : 0.0f;
+                v[j + 2] = m4.z > 0.0f ? v[j + 2] : 0.0f;
+                v[j + 3] = m4.w > 0.0f ? v[j + 3] : 0.0f;
+              }
+            } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) crow[col0 + j] = v[j];
-        }
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) v[j] = __ldg(mrow + j) > 0.0f ? v[j] : 0.0f;
+            }
+          }
+          if (p.c) {
+            float* crow = p.c + roff;
+            if (vec_ok && full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(crow + col0 + j) =
+                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) crow[col0 + j] = v[j];
+            }
+          }
+          if (p.c_hi) {
+            float hv[32], lv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t h = f32_to_tf32_rna(v[j]);
+              hv[j] = __uint_as_float(h);
+              lv[j] = __uint_as_float(f32_to_tf32_rna(v[j] - hv[j]));
+            }
+            float* hrow = p.c_hi + roff;
+            float* lrow = p.c_lo ? p.c_lo + roff : nullptr;
+            if (vec_ok && full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                *reinterpret_cast<float4*>(hrow + col0 + j) =
+                    make_float4(hv[j], hv[j + 1], hv[j + 2], hv[j + 3]);
+                if (lrow)
+                  *reinterpret_cast<float4*>(lrow + col0 + j) =
+                      make_float4(lv[j], lv[j + 1], lv[j + 2], lv[j + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) {
+                  hrow[col0 + j] = hv[j];
+                  if (lrow) lrow[col0 + j] = lv[j];
+                }
+            }
+          }
         }
       }
       tc_fence_before();
@@ -348,10 +439,10 @@ cudaError_t launch_split(const float* src, int64_t ld, bool kcontig, int R, int 
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-template <int PASSES>
+template <int PASSES, bool AK, bool BKM>
 cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                       const CUtensorMap& bl, const TcParams& p, int grid, cudaStream_t s) {
-  auto kern = tc_gemm_kernel<PASSES>;
+  auto kern = tc_gemm_kernel<PASSES, AK, BKM>;
   static unsigned configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -366,6 +457,35 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
   return cudaGetLastError();
 }
 
+template <int PASSES>
+cudaError_t launch_tc_major(bool ak, bool bkm, const CUtensorMap& ah, const CUtensorMap& al,
+                            const CUtensorMap& bh, const CUtensorMap& bl, const TcParams& p,
+                            int grid, cudaStream_t s) {
+  if (ak && bkm) return launch_tc<PASSES, true, true>(ah, al, bh, bl, p, grid, s);
+  if (ak) return launch_tc<PASSES, true, false>(ah, al, bh, bl, p, grid, s);
+  if (bkm) return launch_tc<PASSES, false, true>(ah, al, bh, bl, p, grid, s);
+  return launch_tc<PASSES, false, false>(ah, al, bh, bl, p, grid, s);
+}
+
+// Tensor map of one split copy.  K-major: element (r, k) at base[r*ld + k],
+// box 16 k x rows, 64-byte swizzle.  MN-major: element (r, k) at
+// base[k*ld + r], box 32 mn x 16 k, 128-byte swizzle of 32-byte atoms.
+bool operand_map(CUtensorMap* m, const float* base, bool kmajor, int R, int K, int64_t ld,
+                 int rows_tile) {
+  if (kmajor)
+    return make_tmap_2d(m, base, K, R, ld * 4, kBK, rows_tile, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (R % 32 == 0) {
+    // dims (32 mn, K, R/32 chunks): one copy brings a whole MN-major tile, in
+    // the chunk-after-chunk order the MMA descriptors expect; rows past R
+    // fall in chunks past R/32 and read as zeros.
+    const uint64_t dims[3] = {32, static_cast<uint64_t>(K), static_cast<uint64_t>(R / 32)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 4, 128};
+    const uint32_t box[3] = {32, static_cast<uint32_t>(kBK), static_cast<uint32_t>(rows_tile / 32)};
+    return make_tmap_3d(m, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  }
+  return make_tmap_2d(m, base, R, K, ld * 4, 32, kBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
 }  // namespace
 
 // Workspace bytes tc_gemm needs for the split operands of this shape.
@@ -374,6 +494,48 @@ size_t tc_gemm_workspace_bytes(const GemmArgs& g, int passes) {
   const size_t copies = passes == 3 ? 2 : 1;
   return copies * (align256(static_cast<size_t>(g.M) * kp * 4) +
                    align256(static_cast<size_t>(g.N) * kp * 4));
+}
+
+int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
+                  const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s) {
+  if (M == 0 || N == 0) return kOk;
+  if (K <= 0 || (passes != 1 && passes != 3)) return kErrInvalid;
+  if (!A.hi || !B.hi || (passes == 3 && (!A.lo || !B.lo))) return kErrInvalid;
+  if (!E.c && !E.c_hi) return kErrInvalid;
+  CUtensorMap tah{}, tal{}, tbh{}, tbl{};
+  bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM) &&
+            operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN);
+  if (passes == 3)
+    ok = ok && operand_map(&tal, A.lo, A.kmajor, M, K, A.ld, kBM) &&
+         operand_map(&tbl, B.lo, B.kmajor, N, K, B.ld, kBN);
+  else {
+    tal = tah;
+    tbl = tbh;
+  }
+  if (!ok) return kErrUnsupported;
+  TcParams p{};
+  p.c = E.c; p.bias = E.bias; p.mask = E.mask; p.c_hi = E.c_hi; p.c_lo = E.c_lo;
+  p.status = L.status; p.ldc = E.ldc; p.ldm = E.ldm;
+  p.M = M; p.N = N; p.K = K;
+  p.tiles_m = (M + kBM - 1) / kBM;
+  p.tiles_n = (N + kBN - 1) / kBN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.alpha = E.alpha; p.beta = E.beta; p.relu = E.relu;
+  p.timeout_ns = L.timeout_ns;
+  p.a_map3d = !A.kmajor && M % 32 == 0;
+  p.b_map3d = !B.kmajor && N % 32 == 0;
+  const int grid = std::min(p.num_tiles, L.num_sms);
+  cudaError_t e = passes == 3
+      ? launch_tc_major<3>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid, s)
+      : launch_tc_major<1>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid, s);
+  return e == cudaSuccess ? kOk : cuda_status(e);
+}
+
+int split_tf32(Context* ctx, const float* src, int64_t ld, int rows, int cols, float* hi,
+               float* lo, int64_t ld_out, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return kOk;
+  // a row-major [rows][cols] matrix is its own K-contiguous view (R=rows, K=cols)
+  return cuda_status(launch_split(src, ld, true, rows, cols, ld_out, hi, lo, ctx->num_sms, s));
 }
 
 int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
@@ -399,31 +561,11 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (e != cudaSuccess) return cuda_status(e);
   e = launch_split(g.b, g.ldb, g.tb != 0, g.N, g.K, Kp, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
-
-  CUtensorMap tah{}, tal{}, tbh{}, tbl{};
-  bool ok = make_tmap_2d(&tah, a_hi, g.K, g.M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
-            make_tmap_2d(&tbh, b_hi, g.K, g.N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B);
-  if (passes == 3)
-    ok = ok && make_tmap_2d(&tal, a_lo, g.K, g.M, Kp * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B) &&
-         make_tmap_2d(&tbl, b_lo, g.K, g.N, Kp * 4, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_64B);
-  else {
-    tal = tah;
-    tbl = tbh;
-  }
-  if (!ok) return kErrUnsupported;
-
-  TcParams p{};
-  p.c = g.c; p.bias = g.bias; p.status = ctx->status; p.ldc = g.ldc;
-  p.M = g.M; p.N = g.N; p.K = g.K;
-  p.tiles_m = (g.M + kBM - 1) / kBM;
-  p.tiles_n = (g.N + kBN - 1) / kBN;
-  p.num_tiles = p.tiles_m * p.tiles_n;
-  p.alpha = g.alpha; p.beta = g.beta; p.relu = g.relu;
-  p.timeout_ns = ctx->timeout_ns;
-  const int grid = std::min(p.num_tiles, ctx->num_sms);
-  e = passes == 3 ? launch_tc<3>(tah, tal, tbh, tbl, p, grid, s)
-                  : launch_tc<1>(tah, tal, tbh, tbl, p, grid, s);
-  return e == cudaSuccess ? kOk : cuda_status(e);
+  TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  SplitOperand A{a_hi, a_lo, Kp, true}, B{b_hi, b_lo, Kp, true};
+  TcEpilogue E{};
+  E.c = g.c; E.ldc = g.ldc; E.alpha = g.alpha; E.beta = g.beta; E.bias = g.bias; E.relu = g.relu;
+  return tc_gemm_split(L, A, B, E, g.M, g.N, g.K, passes, s);
 }
 
 }  // namespace mx
@@ -550,6 +692,6 @@ extern "C" __attribute__((visibility("default"))) int32_t mx_gemm_3xtf32_noalloc
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = alpha; p.beta = beta; p.relu = g.relu;
   p.timeout_ns = 2000000000ull;
-  e = launch_tc<3>(tah, tal, tbh, tbl, p, std::min(p.num_tiles, d->num_sms), s);
+  e = launch_tc<3, true, true>(tah, tal, tbh, tbl, p, std::min(p.num_tiles, d->num_sms), s);
   return e == cudaSuccess ? kOk : cuda_status(e);
 }

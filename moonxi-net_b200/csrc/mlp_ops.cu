@@ -81,6 +81,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // block's partial loss (sum of its rows' -log p[label]) to partial[block].
 __global__ void softmax_ce_kernel(const float* __restrict__ logits,
                                   const float* __restrict__ labels, float* __restrict__ grad,
+                                  float* __restrict__ g_hi, float* __restrict__ g_lo,
                                   float* __restrict__ partial, int batch, int C, float denom) {
   __shared__ float row_loss[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,7 +108,14 @@ __global__ void softmax_ce_kernel(const float* __restrict__ logits,
         const float sm =
             __fdiv_rn(static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))), se);
         const float t = (j == label) ? 1.0f : 0.0f;
-        g[j] = __fdiv_rn(__fsub_rn(sm, t), denom);
+        const float gv = __fdiv_rn(__fsub_rn(sm, t), denom);
+        g[j] = gv;
+        if (g_hi) {  // 3xTF32 split of the gradient for the backward GEMMs
+          const int64_t o = static_cast<int64_t>(b) * C + j;
+          const float h = __uint_as_float(f32_to_tf32_rna(gv));
+          g_hi[o] = h;
+          g_lo[o] = __uint_as_float(f32_to_tf32_rna(gv - h));
+        }
       }
     }
   }
@@ -157,7 +165,8 @@ __global__ void norm_sq_kernel(const float* __restrict__ g, int64_t n, float* __
 // v = momentum*v + g*clip + wd*p ; p = p - lr*v  (nparray/trait_impl.mbt:298-308).
 __global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict__ g,
                                   float* __restrict__ v, int64_t n, float lr, float momentum,
-                                  float wd, float max_norm, const float* __restrict__ norm) {
+                                  float wd, float max_norm, const float* __restrict__ norm,
+                                  float* __restrict__ p_hi, float* __restrict__ p_lo) {
   const float nv = *norm;
   const float clip = nv > max_norm ? __fdiv_rn(max_norm, nv) : 1.0f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -165,7 +174,13 @@ __global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict
     const float cg = __fmul_rn(g[i], clip);
     const float vn = __fadd_rn(__fadd_rn(__fmul_rn(momentum, v[i]), cg), __fmul_rn(wd, p[i]));
     v[i] = vn;
-    p[i] = __fsub_rn(p[i], __fmul_rn(lr, vn));
+    const float pn = __fsub_rn(p[i], __fmul_rn(lr, vn));
+    p[i] = pn;
+    if (p_hi) {  // 3xTF32 split of the updated parameters for the next step
+      const float h = __uint_as_float(f32_to_tf32_rna(pn));
+      p_hi[i] = h;
+      p_lo[i] = __uint_as_float(f32_to_tf32_rna(pn - h));
+    }
   }
 }
 
@@ -255,7 +270,8 @@ int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int 
 }
 
 int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
-                      float* loss, int batch, int C, int denom, cudaStream_t s) {
+                      float* loss, int batch, int C, int denom, cudaStream_t s, float* g_hi,
+                      float* g_lo) {
   if (batch <= 0 || C <= 0) return kErrInvalid;
   if (nparray_order(ctx)) {
     int rc = ensure_small_scratch(ctx, static_cast<size_t>(batch) * sizeof(float));
@@ -274,7 +290,7 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
   int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks) * sizeof(float));
   if (rc != kOk) return rc;
   float* partial = static_cast<float*>(ctx->small_scratch);
-  softmax_ce_kernel<<<blocks, 256, 0, s>>>(logits, labels, grad, partial, batch, C,
+  softmax_ce_kernel<<<blocks, 256, 0, s>>>(logits, labels, grad, g_hi, g_lo, partial, batch, C,
                                            static_cast<float>(denom));
   note_launches(1);
   cudaError_t e = cudaGetLastError();
@@ -289,7 +305,7 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
 
 int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
                           float momentum, float wd, float max_norm, float* norm_out,
-                          cudaStream_t s) {
+                          cudaStream_t s, float* p_hi, float* p_lo) {
   if (n <= 0) return kOk;
   const int blocks = grid_for(n, ctx->num_sms, 4);
   int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks + 1) * sizeof(float));
@@ -305,7 +321,7 @@ int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int6
     note_launches(3);  // norm_sq, finish_sum, sgd_update
   }
   sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
-                                                              max_norm, norm);
+                                                              max_norm, norm, p_hi, p_lo);
   return cuda_status(cudaGetLastError());
 }
 

@@ -65,20 +65,63 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s);
 
 size_t tc_gemm_workspace_bytes(const GemmArgs& g, int passes);
 
+// tcgen05 GEMM on operands already in split form.
+struct TcLaunch {
+  int num_sms;
+  int* status;
+  uint64_t timeout_ns;
+};
+// One operand in hi/lo split form (lo may be null for passes = 1).
+// kmajor: element (r, k) at hi[r * ld + k]; else at hi[k * ld + r].
+struct SplitOperand {
+  const float* hi;
+  const float* lo;
+  int64_t ld;
+  bool kmajor;
+};
+// Epilogue: v = alpha*acc (+ beta*c) (+ bias[col]), ReLU if relu, zeroed
+// where mask[row*ldm+col] <= 0 if mask; written to c (if non-null) and as
+// hi/lo split to c_hi/c_lo (if non-null), all with leading dimension ldc.
+struct TcEpilogue {
+  float* c = nullptr;
+  int64_t ldc = 0;
+  float alpha = 1.0f, beta = 0.0f;
+  const float* bias = nullptr;
+  int relu = 0;
+  const float* mask = nullptr;
+  int64_t ldm = 0;
+  float* c_hi = nullptr;
+  float* c_lo = nullptr;
+};
+int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
+                  const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s);
+// hi/lo split of a row-major [rows][cols] matrix (leading dimension ld) into
+// hi/lo with leading dimension ld_out.
+int split_tf32(Context* ctx, const float* src, int64_t ld, int rows, int cols, float* hi,
+               float* lo, int64_t ld_out, cudaStream_t s);
+
 // Adjacent ops of the training step (mlp_ops.cu).
 int relu_backward(Context* ctx, const float* g, const float* x, float* out, int64_t n,
                   cudaStream_t s);
 int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int rows,
                        cudaStream_t s);
+// g_hi/g_lo, p_hi/p_lo (optional): also write the 3xTF32 hi/lo split of the
+// gradient / of the updated parameters (the fast path's operands).
 int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
-                      float* loss, int batch, int C, int denom, cudaStream_t s);
+                      float* loss, int batch, int C, int denom, cudaStream_t s,
+                      float* g_hi = nullptr, float* g_lo = nullptr);
 int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
                           float momentum, float wd, float max_norm, float* norm_out,
-                          cudaStream_t s);
+                          cudaStream_t s, float* p_hi = nullptr, float* p_lo = nullptr);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle);
+
+// 3-D variant (dims and box innermost first; strides of dims 1 and 2).
+bool make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3],
+                  const uint64_t strides_bytes[2], const uint32_t box[3],
                   CUtensorMapSwizzle swizzle);
 
 int cuda_status(cudaError_t e);

@@ -100,6 +100,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3-D tiled bulk tensor load (x innermost).  No cluster multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- cp.async
 // 4-byte async copy with zero fill: copies `src_bytes` (0 or 4) bytes.
 __device__ __forceinline__ void cp_async_4(void* dst, const void* src, uint32_t src_bytes) {
@@ -185,12 +195,29 @@ __device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr, uint32_t sbo_by
   return d;
 }
 
-// Instruction descriptor for kind::tf32 with fp32 accumulation, both
-// operands K-major, dense.
-__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+// UMMA shared-memory descriptor for an MN-major operand tile: 16-byte groups
+// contiguous along MN, swizzle-span-wide MN chunks `lbo_bytes` apart, 8-deep
+// K groups `sbo_bytes` apart.
+__device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t saddr, uint32_t lbo_bytes,
+                                                  uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);             // start address
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;     // LBO: next MN chunk
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;     // SBO: next K group
+  d |= static_cast<uint64_t>(1u) << 46;                             // sm100 descriptor
+  d |= static_cast<uint64_t>(layout & 7u) << 61;                    // swizzle mode
+  return d;
+}
+
+// Instruction descriptor for kind::tf32 with fp32 accumulation, dense;
+// a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn = false,
+                                                  bool b_mn = false) {
   return (1u << 4)                                   // D format: f32
          | (2u << 7)                                 // A format: tf32
          | (2u << 10)                                // B format: tf32
+         | ((a_mn ? 1u : 0u) << 15)                  // A major: 0 K, 1 MN
+         | ((b_mn ? 1u : 0u) << 16)                  // B major: 0 K, 1 MN
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }

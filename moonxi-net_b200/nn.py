@@ -101,7 +101,7 @@ class MLP:
     def __init__(self, dims, weights=None, biases=None, layout: str = "nn", device=None,
                  precision="default", lr: float = 0.01, momentum: float = 0.9,
                  weight_decay: float = 1e-4, max_grad_norm: float = 35.0,
-                 process_group=None):
+                 process_group=None, fused=None):
         if layout not in ("nn", "nt"):
             raise ValueError("layout must be 'nn' (w [in,out]) or 'nt' (w [out,in])")
         self.dims = list(dims)
@@ -137,6 +137,15 @@ class MLP:
         self.b = [self._view(self.params, i, False) for i in range(self.L)]
         self.gw = [self._view(self.grads, i, True) for i in range(self.L)]
         self.gb = [self._view(self.grads, i, False) for i in range(self.L)]
+        # Split-form path (3xTF32 with every operand kept as hi/lo copies written
+        # by its producer): needs TMA-legal leading dimensions (multiples of 4).
+        self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
+                      and fused is not False)
+        if self.fused:
+            self.params_hi = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+            self.params_lo = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+            self.w_hi = [self._view(self.params_hi, i, True) for i in range(self.L)]
+            self.w_lo = [self._view(self.params_lo, i, True) for i in range(self.L)]
         if weights is not None:
             self.load(weights, biases)
         self._bufs = {}
@@ -163,6 +172,8 @@ class MLP:
             if biases is not None:
                 self.b[i].copy_(torch.as_tensor(np.asarray(biases[i], np.float32)))
         self.vels.zero_()
+        if self.fused:
+            ops.split_tf32(self.params, self.params_hi, self.params_lo, ctx=self.ctx)
 
     def weights_numpy(self):
         return ([w.detach().cpu().numpy().copy() for w in self.w],
@@ -190,6 +201,14 @@ class MLP:
             gbuf = [torch.empty((B, self.dims[i + 1]), device=dev, dtype=torch.float32)
                     for i in range(self.L)]
             bufs = (acts, gbuf)
+            if self.fused:
+                def pair(w):
+                    return (torch.empty((B, w), device=dev, dtype=torch.float32),
+                            torch.empty((B, w), device=dev, dtype=torch.float32))
+                # split copies: input, hidden activations, layer gradients
+                bufs = bufs + ([pair(self.dims[0])] + [pair(self.dims[i + 1])
+                                                      for i in range(self.L - 1)],
+                               [pair(self.dims[i + 1]) for i in range(self.L)])
             self._bufs[B] = bufs
         return bufs
 
@@ -209,6 +228,8 @@ class MLP:
         as a 1-element device tensor."""
         B = x.shape[0]
         G = B * self.world if global_batch is None else int(global_batch)
+        if self.fused:
+            return self._step_split(x, labels, B, G, update)
         acts, gbuf = self._buffers(B)
         nt = self.layout == "nt"
         ctx = self.ctx
@@ -262,6 +283,75 @@ class MLP:
             ops.sgd_momentum_autoclip(self.params, self.grads, self.vels, self.lr, self.momentum,
                                       self.weight_decay, self.max_grad_norm, norm_out=self.norm,
                                       ctx=ctx)
+        return self.loss_slot
+
+    def _step_split(self, x, labels, B, G, update):
+        """The step with every GEMM operand in split form, each split copy
+        written once by the kernel that produces the value: the input by one
+        split pass, activations by the forward GEMM epilogue, gradients by
+        the CE kernel and the dX GEMM epilogue (which also applies the ReLU
+        mask of the layer below), weights by the optimizer.  Same arithmetic
+        as the per-call 3xTF32 path, without its per-GEMM prepasses."""
+        acts, gbuf, hsplit, gsplit = self._buffers(B)
+        nt = self.layout == "nt"
+        ctx = self.ctx
+        timer = self.gemm_timer
+        d = self.dims
+
+        def gemm(flops, **k):
+            if timer is None:
+                return ops.gemm_split(ctx=ctx, **k)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ops.gemm_split(ctx=ctx, **k)
+            e1.record()
+            timer.append((flops, e0, e1))
+
+        xh, xl = hsplit[0]
+        ops.split_tf32(x, xh, xl, ctx=ctx)
+        # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
+        for i in range(self.L):
+            last = i + 1 == self.L
+            ah, al = hsplit[i]
+            ch, cl = (None, None) if last else hsplit[i + 1]
+            gemm(2 * B * d[i] * d[i + 1], a_hi=ah, a_lo=al, lda=d[i], a_kmajor=True,
+                 b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=d[i] if nt else d[i + 1],
+                 b_kmajor=nt, M=B, K=d[i], N=d[i + 1], c=acts[i], c_hi=ch, c_lo=cl,
+                 bias=self.b[i], relu=not last)
+        gh, gl = gsplit[self.L - 1]
+        ops.softmax_ce_labels_split(acts[self.L - 1], labels, gbuf[self.L - 1], gh, gl,
+                                    self.loss_slot, G, ctx=ctx)
+        works = []
+        for i in reversed(range(self.L)):
+            fi, fo = d[i], d[i + 1]
+            g = gbuf[i]
+            gh, gl = gsplit[i]
+            hh, hl = hsplit[i]
+            ops.reduce_sum_leading(g, out=self.gb[i], ctx=ctx)
+            if nt:   # dW[out,in] = dY^T X
+                gemm(2 * B * fi * fo, a_hi=gh, a_lo=gl, lda=fo, a_kmajor=False, b_hi=hh,
+                     b_lo=hl, ldb=fi, b_kmajor=False, M=fo, K=B, N=fi, c=self.gw[i])
+            else:    # dW[in,out] = X^T dY
+                gemm(2 * B * fi * fo, a_hi=hh, a_lo=hl, lda=fi, a_kmajor=False, b_hi=gh,
+                     b_lo=gl, ldb=fo, b_kmajor=False, M=fi, K=B, N=fo, c=self.gw[i])
+            if self.pg is not None:
+                import torch.distributed as dist
+                works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
+            if i > 0:
+                # dX = (dY W^T) masked by relu'(h_i); split copy for the next GEMMs
+                ph, pl = gsplit[i - 1]
+                gemm(2 * B * fi * fo, a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True,
+                     b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=fi if nt else fo,
+                     b_kmajor=not nt, M=B, K=fo, N=fi, c=gbuf[i - 1], c_hi=ph, c_lo=pl,
+                     mask=acts[i - 1], ldm=fi)
+        for wk in works:
+            wk.wait()
+        if update:
+            ops.sgd_momentum_autoclip_split(self.params, self.grads, self.vels, self.params_hi,
+                                            self.params_lo, self.lr, self.momentum,
+                                            self.weight_decay, self.max_grad_norm,
+                                            norm_out=self.norm, ctx=ctx)
         return self.loss_slot
 
     # ------------------------------------------------------------ CUDA graph

@@ -181,6 +181,55 @@ def sgd_momentum_autoclip(params: torch.Tensor, grads: torch.Tensor, vels: torch
     check(rc, "mx_sgd_momentum_autoclip")
 
 
+# ---------------------------------------------------------------- split form
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def split_tf32(src: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor | None, ctx=None,
+               stream=None) -> None:
+    """hi/lo 3xTF32 split of a row-major 2-D (or flat, as one row) tensor."""
+    _check_tensor(src, "src")
+    rows, cols = (src.shape[0], src.shape[1]) if src.dim() == 2 else (1, src.numel())
+    rc = _lib.lib().mx_split_tf32(_handle(ctx, src), src.data_ptr(), rows, cols, cols,
+                                  hi.data_ptr(), _ptr(lo), cols, _stream_ptr(stream))
+    check(rc, "mx_split_tf32")
+
+
+def gemm_split(a_hi, a_lo, lda: int, a_kmajor: bool, b_hi, b_lo, ldb: int, b_kmajor: bool,
+               M: int, K: int, N: int, c=None, c_hi=None, c_lo=None, ldc: int | None = None,
+               alpha: float = 1.0, beta: float = 0.0, bias=None, relu: bool = False,
+               mask=None, ldm: int = 0, passes: int = 3, ctx=None, stream=None) -> None:
+    """tcgen05 GEMM on split operands (mx_gemm_split_ex); see the header."""
+    ref = c if c is not None else c_hi
+    rc = _lib.lib().mx_gemm_split_ex(
+        _handle(ctx, a_hi), a_hi.data_ptr(), _ptr(a_lo), lda, int(a_kmajor), b_hi.data_ptr(),
+        _ptr(b_lo), ldb, int(b_kmajor), _ptr(c), _ptr(c_hi), _ptr(c_lo),
+        N if ldc is None else ldc, M, K, N, float(alpha), float(beta), _ptr(bias), int(relu),
+        _ptr(mask), ldm, passes, _stream_ptr(stream))
+    check(rc, "mx_gemm_split_ex")
+    return ref
+
+
+def softmax_ce_labels_split(logits, labels, grad, g_hi, g_lo, loss, denom: int, ctx=None,
+                            stream=None) -> None:
+    B, C = logits.shape
+    rc = _lib.lib().mx_softmax_ce_labels_split(
+        _handle(ctx, logits), logits.data_ptr(), labels.data_ptr(), grad.data_ptr(),
+        g_hi.data_ptr(), g_lo.data_ptr(), _ptr(loss), B, C, int(denom), _stream_ptr(stream))
+    check(rc, "mx_softmax_ce_labels_split")
+
+
+def sgd_momentum_autoclip_split(params, grads, vels, p_hi, p_lo, lr, momentum, weight_decay,
+                                max_grad_norm, norm_out=None, ctx=None, stream=None) -> None:
+    n = params.numel()
+    rc = _lib.lib().mx_sgd_momentum_autoclip_split(
+        _handle(ctx, params), params.data_ptr(), grads.data_ptr(), vels.data_ptr(), n,
+        float(lr), float(momentum), float(weight_decay), float(max_grad_norm), _ptr(norm_out),
+        p_hi.data_ptr(), p_lo.data_ptr(), _stream_ptr(stream))
+    check(rc, "mx_sgd_momentum_autoclip_split")
+
+
 def status(device: int | None = None) -> tuple[int, int]:
     """(status, call site) of the device status word; synchronises, clears it."""
     where = ctypes.c_int32(0)

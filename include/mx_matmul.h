@@ -117,14 +117,17 @@ int32_t mx_split_tf32(void* handle, const float* src, int32_t rows, int32_t cols
  * to c_hi/c_lo (leading dimension ldc).  a_kmajor = 1: A(m,k) at
  * a[m*lda + k]; 0: at a[k*lda + m] (B likewise with n).  passes = 3: 3xTF32
  * (a_lo/b_lo used), 1: TF32.  Base pointers and leading dimensions must be
- * 16-byte multiples (TMA); M, N, K >= 1.  Used by the Linear/MLP step for
- * X W, dY W^T and X^T dY (grad/blas.mbt:35,37) without any transpose. */
+ * 16-byte multiples (TMA); M, N, K >= 1.  flags bit 0 (A) / bit 1 (B): the
+ * MN-major copies stay readable for 32 floats past their last row, which lets
+ * the kernel fetch whole 32-wide chunks when M (N) is not a multiple of 32.
+ * Used by the Linear/MLP step for X W, dY W^T and X^T dY (grad/blas.mbt:35,37)
+ * without any transpose. */
 int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo, int64_t lda,
                          int32_t a_kmajor, const float* b_hi, const float* b_lo, int64_t ldb,
                          int32_t b_kmajor, float* c, float* c_hi, float* c_lo, int64_t ldc,
                          int32_t M, int32_t K, int32_t N, float alpha, float beta,
                          const float* bias, int32_t relu, const float* mask, int64_t ldm,
-                         int32_t passes, void* stream);
+                         int32_t passes, int32_t flags, void* stream);
 
 /* Allocation-free 3xTF32 GEMM.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory inside a library call --

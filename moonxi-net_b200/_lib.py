@@ -54,7 +54,7 @@ SIGNATURES = {
     "mx_split_tf32": (_i32, [_vp, _vp, _i32, _i32, _i64, _vp, _vp, _i64, _vp]),
     "mx_gemm_split_ex": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i32, _vp, _vp, _vp,
                                 _i64, _i32, _i32, _i32, _f32, _f32, _vp, _i32, _vp, _i64, _i32,
-                                _vp]),
+                                _i32, _vp]),
     "mx_softmax_ce_labels_split": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                           _vp]),
     "mx_sgd_momentum_autoclip_split": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32,

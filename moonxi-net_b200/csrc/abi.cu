@@ -342,7 +342,7 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
                                    float* c_hi, float* c_lo, int64_t ldc, int32_t M, int32_t K,
                                    int32_t N, float alpha, float beta, const float* bias,
                                    int32_t relu, const float* mask, int64_t ldm, int32_t passes,
-                                   void* stream) {
+                                   int32_t flags, void* stream) {
   Context* ctx = resolve(handle);
   if (!ctx) return MX_ERR_NO_DEVICE;
   if (M < 0 || N < 0 || K < 1) return MX_ERR_INVALID;
@@ -350,7 +350,8 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
   if (mask && ldm < N) return MX_ERR_INVALID;
   if (!c_hi && c_lo) return MX_ERR_INVALID;
   TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
-  SplitOperand A{a_hi, a_lo, lda, a_kmajor != 0}, B{b_hi, b_lo, ldb, b_kmajor != 0};
+  SplitOperand A{a_hi, a_lo, lda, a_kmajor != 0, (flags & 1) != 0};
+  SplitOperand B{b_hi, b_lo, ldb, b_kmajor != 0, (flags & 2) != 0};
   TcEpilogue E;
   E.c = c; E.ldc = ldc; E.alpha = alpha; E.beta = beta; E.bias = bias; E.relu = relu ? 1 : 0;
   E.mask = mask; E.ldm = ldm; E.c_hi = c_hi; E.c_lo = c_lo;

@@ -471,14 +471,16 @@ cudaError_t launch_tc_major(bool ak, bool bkm, const CUtensorMap& ah, const CUte
 // box 16 k x rows, 64-byte swizzle.  MN-major: element (r, k) at
 // base[k*ld + r], box 32 mn x 16 k, 128-byte swizzle of 32-byte atoms.
 bool operand_map(CUtensorMap* m, const float* base, bool kmajor, int R, int K, int64_t ld,
-                 int rows_tile) {
+                 int rows_tile, bool padded) {
   if (kmajor)
     return make_tmap_2d(m, base, K, R, ld * 4, kBK, rows_tile, CU_TENSOR_MAP_SWIZZLE_64B);
-  if (R % 32 == 0) {
-    // dims (32 mn, K, R/32 chunks): one copy brings a whole MN-major tile, in
-    // the chunk-after-chunk order the MMA descriptors expect; rows past R
-    // fall in chunks past R/32 and read as zeros.
-    const uint64_t dims[3] = {32, static_cast<uint64_t>(K), static_cast<uint64_t>(R / 32)};
+  if (R % 32 == 0 || padded) {
+    // dims (32 mn, K, ceil(R/32) chunks): one copy brings a whole MN-major
+    // tile, in the chunk-after-chunk order the MMA descriptors expect; chunks
+    // past the last read as zeros.  A partial last chunk (padded operands
+    // only) reads the rows past R from memory; they feed only output
+    // rows/columns that are never stored.
+    const uint64_t dims[3] = {32, static_cast<uint64_t>(K), static_cast<uint64_t>((R + 31) / 32)};
     const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 4, 128};
     const uint32_t box[3] = {32, static_cast<uint32_t>(kBK), static_cast<uint32_t>(rows_tile / 32)};
     return make_tmap_3d(m, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
@@ -503,11 +505,11 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   if (!A.hi || !B.hi || (passes == 3 && (!A.lo || !B.lo))) return kErrInvalid;
   if (!E.c && !E.c_hi) return kErrInvalid;
   CUtensorMap tah{}, tal{}, tbh{}, tbl{};
-  bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM) &&
-            operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN);
+  bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM, A.padded) &&
+            operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN, B.padded);
   if (passes == 3)
-    ok = ok && operand_map(&tal, A.lo, A.kmajor, M, K, A.ld, kBM) &&
-         operand_map(&tbl, B.lo, B.kmajor, N, K, B.ld, kBN);
+    ok = ok && operand_map(&tal, A.lo, A.kmajor, M, K, A.ld, kBM, A.padded) &&
+         operand_map(&tbl, B.lo, B.kmajor, N, K, B.ld, kBN, B.padded);
   else {
     tal = tah;
     tbl = tbh;
@@ -522,8 +524,8 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = E.alpha; p.beta = E.beta; p.relu = E.relu;
   p.timeout_ns = L.timeout_ns;
-  p.a_map3d = !A.kmajor && M % 32 == 0;
-  p.b_map3d = !B.kmajor && N % 32 == 0;
+  p.a_map3d = !A.kmajor && (M % 32 == 0 || A.padded);
+  p.b_map3d = !B.kmajor && (N % 32 == 0 || B.padded);
   const int grid = std::min(p.num_tiles, L.num_sms);
   cudaError_t e = passes == 3
       ? launch_tc_major<3>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid, s)

@@ -78,6 +78,10 @@ struct SplitOperand {
   const float* lo;
   int64_t ld;
   bool kmajor;
+  // MN-major only: memory stays readable for at least 32 floats past the
+  // last row of every copy, so whole 32-row chunks may be read (the rows
+  // past the operand feed only output rows/columns that are not stored).
+  bool padded = false;
 };
 // Epilogue: v = alpha*acc (+ beta*c) (+ bias[col]), ReLU if relu, zeroed
 // where mask[row*ldm+col] <= 0 if mask; written to c (if non-null) and as

@@ -142,8 +142,12 @@ class MLP:
         self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
                       and fused is not False)
         if self.fused:
-            self.params_hi = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
-            self.params_lo = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+            # (+_ALIGN: every split copy keeps readable memory past its last
+            # row, so MN-major tiles are fetched as whole 32-wide chunks)
+            self.params_hi = torch.zeros(self.n_flat + _ALIGN, device=dev,
+                                         dtype=torch.float32)[:self.n_flat]
+            self.params_lo = torch.zeros(self.n_flat + _ALIGN, device=dev,
+                                         dtype=torch.float32)[:self.n_flat]
             self.w_hi = [self._view(self.params_hi, i, True) for i in range(self.L)]
             self.w_lo = [self._view(self.params_lo, i, True) for i in range(self.L)]
         if weights is not None:
@@ -202,9 +206,10 @@ class MLP:
                     for i in range(self.L)]
             bufs = (acts, gbuf)
             if self.fused:
-                def pair(w):
-                    return (torch.empty((B, w), device=dev, dtype=torch.float32),
-                            torch.empty((B, w), device=dev, dtype=torch.float32))
+                def pair(w):  # padded past the last row (see params_hi)
+                    return tuple(torch.empty(B * w + _ALIGN, device=dev,
+                                             dtype=torch.float32)[:B * w].view(B, w)
+                                 for _ in range(2))
                 # split copies: input, hidden activations, layer gradients
                 bufs = bufs + ([pair(self.dims[0])] + [pair(self.dims[i + 1])
                                                       for i in range(self.L - 1)],
@@ -300,11 +305,11 @@ class MLP:
 
         def gemm(flops, **k):
             if timer is None:
-                return ops.gemm_split(ctx=ctx, **k)
+                return ops.gemm_split(ctx=ctx, padded=3, **k)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            ops.gemm_split(ctx=ctx, **k)
+            ops.gemm_split(ctx=ctx, padded=3, **k)
             e1.record()
             timer.append((flops, e0, e1))
 

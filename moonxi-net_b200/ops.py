@@ -199,14 +199,17 @@ def split_tf32(src: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor | None, ctx
 def gemm_split(a_hi, a_lo, lda: int, a_kmajor: bool, b_hi, b_lo, ldb: int, b_kmajor: bool,
                M: int, K: int, N: int, c=None, c_hi=None, c_lo=None, ldc: int | None = None,
                alpha: float = 1.0, beta: float = 0.0, bias=None, relu: bool = False,
-               mask=None, ldm: int = 0, passes: int = 3, ctx=None, stream=None) -> None:
-    """tcgen05 GEMM on split operands (mx_gemm_split_ex); see the header."""
+               mask=None, ldm: int = 0, passes: int = 3, padded: int = 0, ctx=None,
+               stream=None) -> None:
+    """tcgen05 GEMM on split operands (mx_gemm_split_ex); see the header.
+    padded: bit 0 / bit 1 when A / B copies have 32 readable floats past
+    their last row."""
     ref = c if c is not None else c_hi
     rc = _lib.lib().mx_gemm_split_ex(
         _handle(ctx, a_hi), a_hi.data_ptr(), _ptr(a_lo), lda, int(a_kmajor), b_hi.data_ptr(),
         _ptr(b_lo), ldb, int(b_kmajor), _ptr(c), _ptr(c_hi), _ptr(c_lo),
         N if ldc is None else ldc, M, K, N, float(alpha), float(beta), _ptr(bias), int(relu),
-        _ptr(mask), ldm, passes, _stream_ptr(stream))
+        _ptr(mask), ldm, passes, int(padded), _stream_ptr(stream))
     check(rc, "mx_gemm_split_ex")
     return ref
 

@@ -37,14 +37,21 @@ def test_split_tf32_matches_rounding_rule(cuda_device):
 
 
 def _split(t):
-    hi, lo = torch.empty_like(t), torch.empty_like(t)
+    # 64 readable floats past the last row, as the `padded` flag requires
+    def padded_like(x):
+        return torch.full((x.numel() + 64,), float("nan"), device="cuda")[:x.numel()].view(x.shape)
+    hi, lo = padded_like(t), padded_like(t)
     ops.split_tf32(t, hi, lo)
     return hi, lo
 
 
+@pytest.mark.parametrize("padded", [0, 3])
 @pytest.mark.parametrize("a_k", [True, False])
 @pytest.mark.parametrize("b_k", [True, False])
-def test_gemm_split_all_majors_with_mask_and_split_out(cuda_device, a_k, b_k):
+def test_gemm_split_all_majors_with_mask_and_split_out(cuda_device, a_k, b_k, padded):
+    """M = 520 and N = 300 are not multiples of 32: MN-major operands take the
+    per-chunk copies (padded = 0) or whole chunks reading the NaN padding past
+    the last row (padded = 3), which must not reach any stored output."""
     M, K, N = 520, 392, 300
     g = torch.Generator("cuda").manual_seed(3)
     A = torch.randn(M, K, device="cuda", generator=g)          # logical A[m, k]
@@ -58,7 +65,7 @@ def test_gemm_split_all_majors_with_mask_and_split_out(cuda_device, a_k, b_k):
     c = torch.empty(M, N, device="cuda")
     ch, cl = torch.empty_like(c), torch.empty_like(c)
     ops.gemm_split(ah, al, K if a_k else M, a_k, bh, bl, K if b_k else N, b_k, M, K, N, c=c,
-                   c_hi=ch, c_lo=cl, bias=bias, mask=mask, ldm=N)
+                   c_hi=ch, c_lo=cl, bias=bias, mask=mask, ldm=N, padded=padded)
     torch.cuda.synchronize()
     ref = (A.double() @ B.double() + bias.double()[None, :]) * (mask > 0)
     scale = A.double().abs() @ B.double().abs() + bias.double().abs()[None, :]

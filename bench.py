@@ -310,17 +310,38 @@ def run_ours(args):
     elapsed = float(t.item())
     value = GLOBAL_BATCH * args.steps / elapsed
 
-    # ---- e2e: public step call with host batch copy and loss read-back
+    # ---- e2e: every step copies its batch from pinned host memory and reads
+    # the loss back.  As a training loop does, the next batch is uploaded on a
+    # copy stream while the current step runs (two input buffers, one
+    # captured step per buffer); the timed region holds every copy and read.
     loss_host = []
+    Xb, Yb = [X, torch.empty_like(X)], [Y, torch.empty_like(Y)]
+    if use_graph:
+        graphs = [model._graph, model.capture(Xb[1], Yb[1], GLOBAL_BATCH)]
+        steps_fn = [graphs[0].replay, graphs[1].replay]
+    else:
+        steps_fn = [lambda: model.step(Xb[0], Yb[0], GLOBAL_BATCH),
+                    lambda: model.step(Xb[1], Yb[1], GLOBAL_BATCH)]
+    copy_stream = torch.cuda.Stream()
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
     barrier()
     e2 = torch.cuda.Event(enable_timing=True)
     e3 = torch.cuda.Event(enable_timing=True)
     e2.record()
-    for _ in range(args.steps):
-        X.copy_(x_pin, non_blocking=True)
-        Y.copy_(y_pin, non_blocking=True)
-        loss = run_step()
-        loss_host.append(float(loss.item()))
+    with torch.cuda.stream(copy_stream):
+        Xb[0].copy_(x_pin, non_blocking=True)
+        Yb[0].copy_(y_pin, non_blocking=True)
+        ready[0].record()
+    for i in range(args.steps):
+        cur, nxt = i % 2, 1 - i % 2
+        if i + 1 < args.steps:  # buffer nxt was last read by step i-1, already done
+            with torch.cuda.stream(copy_stream):
+                Xb[nxt].copy_(x_pin, non_blocking=True)
+                Yb[nxt].copy_(y_pin, non_blocking=True)
+                ready[nxt].record()
+        torch.cuda.current_stream().wait_event(ready[cur])
+        steps_fn[cur]()
+        loss_host.append(float(model.loss_slot.item()))
     e3.record()
     barrier()
     e2e_t = torch.tensor([e2.elapsed_time(e3) / 1e3], device=dev)
@@ -328,8 +349,10 @@ def run_ours(args):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = GLOBAL_BATCH * args.steps / float(e2e_t.item())
     h2d = x_pin.numel() * 4 + y_pin.numel() * 4
-    if use_graph:
+    if use_graph:  # graphs holding NCCL calls go before the process group does
         model.release_graph()
+        del graphs
+    del steps_fn
 
     # ---- GEMM time inside one eager step (roofline of the dominant kernel)
     gemm_log = []
@@ -341,6 +364,15 @@ def run_ours(args):
     g_flops = sum(f for f, _, _ in gemm_log)
     g_time = sum(a.elapsed_time(b_) / 1e3 for _, a, b_ in gemm_log)
     step_gpu_time = elapsed / args.steps
+    # phase boundaries of one more eager step (CUDA events on the step's stream)
+    marks = []
+    model.phase_marks = marks
+    barrier()
+    model.step(X, Y, GLOBAL_BATCH)
+    barrier()
+    model.phase_marks = None
+    phases = {marks[i][0]: round(marks[i - 1][1].elapsed_time(marks[i][1]), 3)
+              for i in range(1, len(marks))}
 
     gemm_bench = {}
     if rank == 0 and world == 1 and not args.skip_gemm:
@@ -404,6 +436,7 @@ def run_ours(args):
             "flop_per_sample": FLOP_PER_SAMPLE,
             "model_tflops": round(value * FLOP_PER_SAMPLE / 1e12, 1),
             "final_loss": loss_host[-1] if loss_host else None,
+            "step_phases_ms_rank0_eager": phases,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:

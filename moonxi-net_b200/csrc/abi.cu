@@ -63,8 +63,10 @@ int init_context(Context* c, int device) {
   cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
   c->precision = env_precision();
   c->sync_check = std::getenv("MX_SYNC_CHECK") ? std::atoi(std::getenv("MX_SYNC_CHECK")) : 0;
-  cudaError_t e = cudaMalloc(&c->status, 2 * sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(c->status, 0, 2 * sizeof(int));
+  // words: [0] status, [1] call site, [2] dynamic tile counter of the GEMMs
+  cudaError_t e = cudaMalloc(&c->status, 4 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, 4 * sizeof(int));
+  c->sched = c->status + 2;
   if (prev != device) cudaSetDevice(prev);
   return cuda_status(e);
 }
@@ -350,6 +352,12 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
   if (mask && ldm < N) return MX_ERR_INVALID;
   if (!c_hi && c_lo) return MX_ERR_INVALID;
   TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  L.sched = ctx->sched;
+  const size_t sk = tc_streamk_bytes(M, N, K, ctx->num_sms);
+  if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
+    L.ws = ctx->workspace;
+    L.ws_bytes = ctx->ws_bytes;
+  }
   SplitOperand A{a_hi, a_lo, lda, a_kmajor != 0, (flags & 1) != 0};
   SplitOperand B{b_hi, b_lo, ldb, b_kmajor != 0, (flags & 2) != 0};
   TcEpilogue E;
@@ -431,8 +439,9 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
   if (!c || M <= 0 || N <= 0 || K < 0) return 0;
   GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
   const int p = resolve_precision(c, M, K, N, precision);
-  if (p == MX_PREC_3XTF32) return tc_gemm_workspace_bytes(g, 3);
-  if (p == MX_PREC_TF32) return tc_gemm_workspace_bytes(g, 1);
+  const size_t sk = tc_streamk_bytes(M, N, K, c->num_sms);
+  if (p == MX_PREC_3XTF32) return tc_gemm_workspace_bytes(g, 3) + sk;
+  if (p == MX_PREC_TF32) return tc_gemm_workspace_bytes(g, 1) + sk;
   if (p == MX_PREC_NPARRAY) return 0;  // no split-K in NpArray order
   return simt_gemm_scratch_bytes(c, g);
 }

@@ -26,6 +26,7 @@
 // abort flag, records kErrTimeout, drains in-flight copies and MMAs, frees
 // TMEM and returns.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "mx_internal.h"
@@ -55,7 +56,7 @@ struct Cfg {
   static constexpr int kOperandCopies = PASSES == 3 ? 2 : 1;
   static constexpr int kStageBytes = kOperandCopies * (kATile + kBTile);
   static constexpr int kStages = PASSES == 3 ? 4 : 8;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
 };
 
 struct TcParams {
@@ -72,6 +73,13 @@ struct TcParams {
   int relu;
   uint64_t timeout_ns;
   bool a_map3d, b_map3d;  // MN-major operand loaded by one 3-D copy per tile
+  // Stream-K: the (tile, k-block) iterations are split evenly over the CTAs;
+  // a tile shared by several CTAs is summed by whichever finishes last.
+  int sk;
+  int sk_tile0;           // first tile of the stream-K region
+  float* sk_partials;     // [2 * gridDim.x][128][256] fp32 partial tiles
+  int* sk_counters;       // [num_tiles] arrival counters, zero at launch
+  int* tile_counter;      // dynamic whole-tile scheduling (zero at launch), or null
 };
 
 // Grouped raster: bands of 16 M-tiles, N-major inside a band, so the CTAs
@@ -84,6 +92,232 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   const int r = t - band * G * tiles_n;
   tm = first_m + r % gm;
   tn = r / gm;
+}
+
+// The sequence of work segments of one CTA: a segment is k-blocks [kb0, kb1)
+// of one tile.  Whole tiles below sk_tile0 go data-parallel (tiles
+// blockIdx.x, +gridDim.x, ...: every CTA runs the same number of them, in
+// lock-step, so concurrent CTAs share k-slices in L2).  In stream-K mode the
+// remaining tiles' iterations (tiles x k-blocks) are then split into equal
+// contiguous shares, one per CTA, cut at tile boundaries.
+// Dynamic whole-tile scheduling (p.tile_counter set): the producer thread
+// takes the next tile from a global atomic counter and publishes its id in a
+// shared-memory ring that the MMA thread and the epilogue warps read in the
+// same order.  A CTA that starts late (its SM busy with another kernel, e.g.
+// an NCCL all-reduce running alongside) simply takes fewer tiles, instead of
+// leaving its fixed share as a tail.
+constexpr int kRing = 4;
+struct TileRing {
+  uint64_t* full;
+  uint64_t* empty;
+  int* tile;
+};
+enum Role { kProducer = 0, kMma = 1, kEpilogue = 2 };
+
+struct SegIter {
+  int64_t g, g_end;  // stream-K iteration cursor
+  int t;             // static data-parallel tile cursor
+  int n;             // dynamic: tiles taken from the ring so far
+  bool dp_done;
+  __device__ __forceinline__ void init(const TcParams& p, int num_kb) {
+    t = blockIdx.x;
+    n = 0;
+    dp_done = false;
+    g = g_end = 0;
+    if (p.sk) {
+      const int64_t base = static_cast<int64_t>(p.sk_tile0) * num_kb;
+      const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
+      g = base + W * blockIdx.x / gridDim.x;
+      g_end = base + W * (blockIdx.x + 1) / gridDim.x;
+    }
+  }
+  // Next whole tile of the data-parallel phase, -1 when the phase is over
+  // (or on abort).
+  template <int ROLE>
+  __device__ __forceinline__ int next_dp(const TcParams& p, const TileRing& ring,
+                                         volatile int* abort_flag) {
+    const int dp_end = p.sk ? p.sk_tile0 : p.num_tiles;
+    if (!p.tile_counter) {
+      if (t >= dp_end) return -1;
+      const int r = t;
+      t += gridDim.x;
+      return r;
+    }
+    const int slot = n % kRing;
+    const uint32_t par = (n / kRing) & 1;
+    ++n;
+    int r;
+    if (ROLE == kProducer) {
+      if (!wait_bar(&ring.empty[slot], par ^ 1, abort_flag, p.status, p.timeout_ns, 205))
+        return -1;
+      r = atomicAdd(p.tile_counter, 1);
+      if (r >= dp_end) r = -1;
+      ring.tile[slot] = r;
+      bar_arrive(&ring.full[slot]);  // release: the id is visible to the waiters
+    } else {
+      if (!wait_bar(&ring.full[slot], par, abort_flag, p.status, p.timeout_ns, 206)) return -1;
+      r = ring.tile[slot];
+      if (ROLE == kEpilogue) bar_arrive(&ring.empty[slot]);
+    }
+    return r;
+  }
+  template <int ROLE>
+  __device__ __forceinline__ bool next(const TcParams& p, int num_kb, int& tile, int& kb0,
+                                       int& kb1, const TileRing& ring, volatile int* abort_flag) {
+    if (!dp_done) {
+      const int r = next_dp<ROLE>(p, ring, abort_flag);
+      if (r >= 0) {
+        tile = r;
+        kb0 = 0;
+        kb1 = num_kb;
+        return true;
+      }
+      dp_done = true;
+      if (*abort_flag) return false;
+    }
+    if (g >= g_end) return false;
+    tile = static_cast<int>(g / num_kb);
+    kb0 = static_cast<int>(g - static_cast<int64_t>(tile) * num_kb);
+    const int64_t left = g_end - g;
+    kb1 = (kb0 + left < num_kb) ? static_cast<int>(kb0 + left) : num_kb;
+    g += kb1 - kb0;
+    return true;
+  }
+};
+
+// Stream-K bookkeeping over the stream-K region (iterations counted from the
+// first stream-K tile, W of them): the CTA whose share holds iteration g, and
+// the first iteration of a CTA's share.
+__device__ __forceinline__ int sk_cta_of(int64_t g, int64_t W, int G) {
+  return static_cast<int>(((g + 1) * G + W - 1) / W) - 1;
+}
+__device__ __forceinline__ int64_t sk_start(int c, int64_t W, int G) { return W * c / G; }
+
+// Epilogue of one 32-column chunk of one output row: v holds alpha-less
+// accumulator values; applies alpha/beta/bias/ReLU/mask, stores c and the
+// hi/lo split.
+__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0,
+                                            const float (&acc)[32], bool vec_ok, bool mask_vec) {
+  const int64_t roff = static_cast<int64_t>(row) * p.ldc;
+  const bool full_chunk = col0 + 32 <= p.N;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = p.alpha * acc[j];
+    const int col = col0 + j;
+    if (col < p.N) {
+      if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col];
+      if (p.bias) x = x + __ldg(p.bias + col);
+      if (p.relu) x = x > 0.0f ? x : 0.0f;
+    }
+    v[j] = x;
+  }
+  if (p.mask) {
+    const float* mrow = p.mask + static_cast<int64_t>(row) * p.ldm + col0;
+    if (mask_vec && full_chunk) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 m4 = __ldg(reinterpret_cast<const float4*>(mrow + j));
+        v[j] = m4.x > 0.0f ? v[j] : 0.0f;
+        v[j + 1] = m4.y > 0.0f ? v[j + 1] : 0.0f;
+        v[j + 2] = m4.z > 0.0f ? v[j + 2] : 0.0f;
+        v[j + 3] = m4.w > 0.0f ? v[j + 3] : 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) v[j] = __ldg(mrow + j) > 0.0f ? v[j] : 0.0f;
+    }
+  }
+  if (p.c) {
+    float* crow = p.c + roff;
+    if (vec_ok && full_chunk) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) crow[col0 + j] = v[j];
+    }
+  }
+  if (p.c_hi) {
+    float hv[32], lv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t h = f32_to_tf32_rna(v[j]);
+      hv[j] = __uint_as_float(h);
+      lv[j] = __uint_as_float(f32_to_tf32_rna(v[j] - hv[j]));
+    }
+    float* hrow = p.c_hi + roff;
+    float* lrow = p.c_lo ? p.c_lo + roff : nullptr;
+    if (vec_ok && full_chunk) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        *reinterpret_cast<float4*>(hrow + col0 + j) = make_float4(hv[j], hv[j + 1], hv[j + 2], hv[j + 3]);
+        if (lrow)
+          *reinterpret_cast<float4*>(lrow + col0 + j) = make_float4(lv[j], lv[j + 1], lv[j + 2], lv[j + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) {
+          hrow[col0 + j] = hv[j];
+          if (lrow) lrow[col0 + j] = lv[j];
+        }
+    }
+  }
+}
+
+// Epilogue of four consecutive outputs (row, col..col+3): the same math as
+// store_chunk for a 4-wide group.
+__device__ __forceinline__ void store_quad(const TcParams& p, int row, int col, float4 acc,
+                                           bool vec_ok, bool mask_vec) {
+  const int64_t roff = static_cast<int64_t>(row) * p.ldc;
+  const bool full = col + 4 <= p.N;
+  float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float x = p.alpha * v[j];
+    if (col + j < p.N) {
+      if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col + j];
+      if (p.bias) x = x + __ldg(p.bias + col + j);
+      if (p.relu) x = x > 0.0f ? x : 0.0f;
+      if (p.mask && !(__ldg(p.mask + static_cast<int64_t>(row) * p.ldm + col + j) > 0.0f)) x = 0.0f;
+    }
+    v[j] = x;
+  }
+  float hv[4], lv[4];
+  if (p.c_hi) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      hv[j] = __uint_as_float(f32_to_tf32_rna(v[j]));
+      lv[j] = __uint_as_float(f32_to_tf32_rna(v[j] - hv[j]));
+    }
+  }
+  if (vec_ok && full) {
+    if (p.c) *reinterpret_cast<float4*>(p.c + roff + col) = make_float4(v[0], v[1], v[2], v[3]);
+    if (p.c_hi) {
+      *reinterpret_cast<float4*>(p.c_hi + roff + col) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+      if (p.c_lo)
+        *reinterpret_cast<float4*>(p.c_lo + roff + col) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (col + j < p.N) {
+        if (p.c) p.c[roff + col + j] = v[j];
+        if (p.c_hi) {
+          p.c_hi[roff + col + j] = hv[j];
+          if (p.c_lo) p.c_lo[roff + col + j] = lv[j];
+        }
+      }
+  }
+  (void)mask_vec;
+}
+
+__device__ __forceinline__ void epilogue_bar() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
 }
 
 // One operand tile (rows x 16 k) of one copy (hi or lo) into shared memory.
@@ -124,8 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + C::kStages;   // [2]
   uint64_t* acc_empty = acc_full + 2;        // [2]
   uint64_t* drain = acc_empty + 2;           // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ring_full = drain + 1;           // [kRing] dynamic tile ids published
+  uint64_t* ring_empty = ring_full + kRing;  // [kRing] ... and consumed
+  int* ring_tile = reinterpret_cast<int*>(ring_empty + kRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_tile + kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  TileRing ring{ring_full, ring_empty, ring_tile};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -139,6 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bar_init(&acc_empty[a], 128);
     }
     bar_init(drain, 1);
+    for (int r = 0; r < kRing; ++r) {
+      bar_init(&ring_full[r], 1);
+      bar_init(&ring_empty[r], 128);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmAh);
@@ -167,10 +409,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool armed[C::kStages];
       for (int s = 0; s < C::kStages; ++s) armed[s] = false;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+      SegIter it;
+      it.init(p, num_kb);
+      int t, kb0, kb1;
+      while (ok && it.next<kProducer>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, abort_flag, p.status, p.timeout_ns, 201)) {
             ok = false;
             break;
@@ -212,9 +457,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+      SegIter it;
+      it.init(p, num_kb);
+      int t, kb0, kb1;
+      while (ok && it.next<kMma>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
         if (!wait_bar(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, p.timeout_ns, 202)) {
           ok = false;
           break;
@@ -222,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         uint32_t accumulate = 0;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&full[stage], phase, abort_flag, p.status, p.timeout_ns, 203)) {
             ok = false;
             break;
@@ -273,16 +522,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         ((reinterpret_cast<uintptr_t>(p.c) | reinterpret_cast<uintptr_t>(p.c_hi) |
           reinterpret_cast<uintptr_t>(p.c_lo)) & 15u) == 0;
     const bool mask_vec = (p.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0);
+    __shared__ int sk_last;  // broadcast of the arrival test among the epilogue warps
+    const int64_t sk_base = static_cast<int64_t>(p.sk_tile0) * num_kb;  // first SK iteration
+    const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
+    const int G = gridDim.x;
+    const int64_t my_start = p.sk ? sk_start(blockIdx.x, W, G) : 0;  // relative to sk_base
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    SegIter it;
+    it.init(p, num_kb);
+    int t, kb0, kb1;
+    while (it.next<kEpilogue>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
       if (!wait_bar(&acc_full[acc], acc_phase, abort_flag, p.status, p.timeout_ns, 204)) break;
       tc_fence_after();
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int row = tm * kBM + row_in_tile;
-      const int64_t roff = static_cast<int64_t>(row) * p.ldc;
+      const bool whole = kb0 == 0 && kb1 == num_kb;
+      // partial tile: this CTA's slot (0: its share starts inside this tile)
+      float* slot = nullptr;
+      if (!whole) {
+        const int64_t tile_g0 = static_cast<int64_t>(t) * num_kb - sk_base;
+        const int sel = my_start >= tile_g0 ? 0 : 1;
+        slot = p.sk_partials + (static_cast<int64_t>(blockIdx.x) * 2 + sel) * (kBM * kBN) +
+               static_cast<int64_t>(row_in_tile) * kBN;
+      }
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         uint32_t r[32];
@@ -291,83 +557,76 @@ __global__ void __launch_bounds__(kThreads, 1)
                            chunk * 32,
                        r);
         tmem_wait_ld();
-        const int col0 = tn * kBN + chunk * 32;
-        if (row < p.M && col0 < p.N) {
-          const bool full_chunk = col0 + 32 <= p.N;
-          float v[32];
+        if (whole) {
+          const int col0 = tn * kBN + chunk * 32;
+          if (row < p.M && col0 < p.N) {
+            float a[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = p.alpha * __uint_as_float(r[j]);
-            const int col = col0 + j;
-            if (col < p.N) {
-              if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col];
-              if (p.bias) x = x + __ldg(p.bias + col);
-              if (p.relu) x = x > 0.0f ? x : 0.0f;
-            }
-            v[j] = x;
+            for (int j = 0; j < 32; ++j) a[j] = __uint_as_float(r[j]);
+            store_chunk(p, row, col0, a, vec_ok, mask_vec);
           }
-          if (p.mask) {
-            const float* mrow = p.mask + static_cast<int64_t>(row) * p.ldm + col0;
-            if (mask_vec && full_chunk) {
+        } else {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 m4 = __ldg(reinterpret_cast<const float4*>(mrow + j));
-                v[j] = m4.x > 0.0f ? v[j] : 0.0f;
-                v[j + 1] = m4.y > 0.0f ? v[j + 1] : 0.0f;
-                v[j + 2] = m4.z > 0.0f ? v[j + 2] : 0.0f;
-                v[j + 3] = m4.w > 0.0f ? v[j + 3] : 0.0f;
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(slot + chunk * 32 + j) =
+                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        }
+      }
+      tc_fence_before();
+      bar_arrive(&acc_empty[acc]);  // TMEM is free again; partials are in memory
+      if (!whole) {
+        // Arrival: the last CTA to finish its part of tile t sums all parts
+        // (in k order, so the result does not depend on who is last) and runs
+        // the epilogue.  Nobody waits for anybody.
+        const int64_t tile_g0 = static_cast<int64_t>(t) * num_kb - sk_base;
+        const int c_first = sk_cta_of(tile_g0, W, G);
+        const int c_last = sk_cta_of(tile_g0 + num_kb - 1, W, G);
+        __threadfence();
+        epilogue_bar();
+        if (row_in_tile == 0) {
+          const int old = atomicAdd(&p.sk_counters[t], 1);
+          sk_last = (old == c_last - c_first) ? 1 : 0;
+          if (sk_last) p.sk_counters[t] = 0;  // ready for the next launch
+        }
+        epilogue_bar();
+        if (sk_last) {
+          __threadfence();
+          // Coalesced pass over the tile: each epilogue thread owns one 4-wide
+          // column group (q) of every other row, so a warp reads 512
+          // contiguous bytes of a partial per load and keeps many in flight.
+          const int q = row_in_tile & 63;
+          const int64_t tile_off = static_cast<int64_t>(row_in_tile >> 6) * kBN + q * 4;
+          const int col = tn * kBN + q * 4;
+#pragma unroll 1
+          for (int i0 = 0; i0 < kBM / 2; i0 += 8) {
+            float4 s[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) s[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int c = c_first; c <= c_last; ++c) {  // k order: same sum on any finisher
+              const int sel = sk_start(c, W, G) >= tile_g0 ? 0 : 1;
+              const float* src = p.sk_partials + (static_cast<int64_t>(c) * 2 + sel) * (kBM * kBN) +
+                                 tile_off + static_cast<int64_t>(i0) * 2 * kBN;
+              float4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                v[u] = __ldcg(reinterpret_cast<const float4*>(src + u * 2 * kBN));
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                s[u].x += v[u].x;
+                s[u].y += v[u].y;
+                s[u].z += v[u].z;
+                s[u].w += v[u].w;
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) v[j] = __ldg(mrow + j) > 0.0f ? v[j] : 0.0f;
             }
-          }
-          if (p.c) {
-            float* crow = p.c + roff;
-            if (vec_ok && full_chunk) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(crow + col0 + j) =
-                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) crow[col0 + j] = v[j];
-            }
-          }
-          if (p.c_hi) {
-            float hv[32], lv[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const uint32_t h = f32_to_tf32_rna(v[j]);
-              hv[j] = __uint_as_float(h);
-              lv[j] = __uint_as_float(f32_to_tf32_rna(v[j] - hv[j]));
-            }
-            float* hrow = p.c_hi + roff;
-            float* lrow = p.c_lo ? p.c_lo + roff : nullptr;
-            if (vec_ok && full_chunk) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                *reinterpret_cast<float4*>(hrow + col0 + j) =
-                    make_float4(hv[j], hv[j + 1], hv[j + 2], hv[j + 3]);
-                if (lrow)
-                  *reinterpret_cast<float4*>(lrow + col0 + j) =
-                      make_float4(lv[j], lv[j + 1], lv[j + 2], lv[j + 3]);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) {
-                  hrow[col0 + j] = hv[j];
-                  if (lrow) lrow[col0 + j] = lv[j];
-                }
+            for (int u = 0; u < 8; ++u) {
+              const int r = tm * kBM + (row_in_tile >> 6) + 2 * (i0 + u);
+              if (r < p.M && col < p.N) store_quad(p, r, col, s[u], vec_ok, mask_vec);
             }
           }
         }
       }
-      tc_fence_before();
-      bar_arrive(&acc_empty[acc]);
     }
   }
 
@@ -526,11 +785,54 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   p.timeout_ns = L.timeout_ns;
   p.a_map3d = !A.kmajor && (M % 32 == 0 || A.padded);
   p.b_map3d = !B.kmajor && (N % 32 == 0 || B.padded);
-  const int grid = std::min(p.num_tiles, L.num_sms);
+  // Fewest CTAs that still finish the tiles in the same number of waves: a
+  // 128- or 512-tile GEMM takes 128 SMs, leaving the rest to a concurrent
+  // NCCL all-reduce at no cost to the GEMM (B200 has 148 SMs).
+  const int waves = (p.num_tiles + L.num_sms - 1) / L.num_sms;
+  int grid = (p.num_tiles + waves - 1) / waves;
+  static const bool dyn_enabled = [] {  // dynamic tile order: opt-in (MX_DYNSCHED=1)
+    const char* e = std::getenv("MX_DYNSCHED");
+    return e && e[0] == '1';
+  }();
+  if (L.sched && dyn_enabled) {
+    p.tile_counter = L.sched;
+    cudaError_t me = cudaMemsetAsync(L.sched, 0, sizeof(int), s);
+    if (me != cudaSuccess) return cuda_status(me);
+  }
+  const size_t sk_need = tc_streamk_bytes(M, N, K, L.num_sms);
+  if (sk_need > 0 && L.ws && L.ws_bytes >= sk_need) {
+    p.sk = 1;
+    p.sk_tile0 = (p.num_tiles / L.num_sms) * L.num_sms;  // full waves stay data-parallel
+    p.sk_partials = static_cast<float*>(L.ws);
+    p.sk_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(L.ws) +
+                                           static_cast<size_t>(2) * L.num_sms * kBM * kBN * 4);
+    grid = L.num_sms;
+    cudaError_t me = cudaMemsetAsync(p.sk_counters, 0, sizeof(int) * p.num_tiles, s);
+    if (me != cudaSuccess) return cuda_status(me);
+  }
   cudaError_t e = passes == 3
       ? launch_tc_major<3>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid, s)
       : launch_tc_major<1>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid, s);
   return e == cudaSuccess ? kOk : cuda_status(e);
+}
+
+size_t tc_streamk_bytes(int M, int N, int K, int num_sms) {
+  static const bool disabled = [] {
+    const char* e = std::getenv("MX_STREAMK");
+    return e && e[0] == '0';
+  }();
+  if (disabled || M <= 0 || N <= 0 || K <= 0 || num_sms <= 0) return 0;
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int num_kb = (K + kBK - 1) / kBK;
+  const int waves = (tiles + num_sms - 1) / num_sms;
+  const double fill = static_cast<double>(tiles) / (static_cast<double>(waves) * num_sms);
+  // Stream-K only pays when whole tiles leave most SMs idle: its CTAs walk
+  // k at staggered offsets, which costs L2 reuse (measured on B200: a
+  // 128-tile GEMM on 148 SMs runs faster data-parallel, a 32-tile one faster
+  // stream-K).  Also each CTA's share must be at least 8 k-blocks.
+  const int rem = tiles % num_sms;
+  if (fill >= 0.5 || static_cast<int64_t>(rem) * num_kb < 8LL * num_sms) return 0;
+  return static_cast<size_t>(2) * num_sms * kBM * kBN * 4 + align256(sizeof(int) * tiles);
 }
 
 int split_tf32(Context* ctx, const float* src, int64_t ld, int rows, int cols, float* hi,
@@ -545,7 +847,9 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (g.K == 0) return simt_gemm(ctx, g, s);
   if (passes != 1 && passes != 3) return kErrInvalid;
   const int64_t Kp = (static_cast<int64_t>(g.K) + 3) & ~static_cast<int64_t>(3);
-  int rc = ensure_workspace(ctx, tc_gemm_workspace_bytes(g, passes));
+  const size_t split_bytes = tc_gemm_workspace_bytes(g, passes);
+  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->num_sms);
+  int rc = ensure_workspace(ctx, split_bytes + sk_bytes);
   if (rc != kOk) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);
   float* a_hi = reinterpret_cast<float*>(ws);
@@ -564,6 +868,9 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   e = launch_split(g.b, g.ldb, g.tb != 0, g.N, g.K, Kp, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
   TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  L.sched = ctx->sched;
+  L.ws = static_cast<uint8_t*>(ctx->workspace) + split_bytes;  // split_bytes is 256-aligned
+  L.ws_bytes = sk_bytes;
   SplitOperand A{a_hi, a_lo, Kp, true}, B{b_hi, b_lo, Kp, true};
   TcEpilogue E{};
   E.c = g.c; E.ldc = g.ldc; E.alpha = g.alpha; E.beta = g.beta; E.bias = g.bias; E.relu = g.relu;

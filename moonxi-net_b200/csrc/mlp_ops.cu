@@ -65,6 +65,52 @@ __global__ void reduce_leading_kernel(const float* __restrict__ in, float* __res
   }
 }
 
+// Two-pass column sums for wide, 16-byte aligned inputs: pass 1 has block
+// (128 columns as float4 x 8 row lanes) per (column block, row split) and
+// writes one partial row per split; pass 2 adds the splits in order.  Every
+// sum has a fixed order, so the result is deterministic.
+__global__ void reduce_leading_part_kernel(const float* __restrict__ in,
+                                           float* __restrict__ partial, int cols, int rows,
+                                           int rows_per) {
+  __shared__ float4 part[8][33];
+  const int q = threadIdx.x & 31, lr = threadIdx.x >> 5;
+  const int col = blockIdx.x * 128 + q * 4;
+  const int r0 = blockIdx.y * rows_per;
+  const int r1 = min(rows, r0 + rows_per);
+  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (col < cols) {
+    for (int r = r0 + lr; r < r1; r += 8) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(in + static_cast<int64_t>(r) * cols + col));
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+  }
+  part[lr][q] = s;
+  __syncthreads();
+  if (lr == 0 && col < cols) {
+    float4 t = part[0][q];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+      t.x += part[k][q].x;
+      t.y += part[k][q].y;
+      t.z += part[k][q].z;
+      t.w += part[k][q].w;
+    }
+    *reinterpret_cast<float4*>(partial + static_cast<int64_t>(blockIdx.y) * cols + col) = t;
+  }
+}
+
+__global__ void reduce_leading_finish_kernel(const float* __restrict__ partial,
+                                             float* __restrict__ out, int cols, int splits) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= cols) return;
+  float s = 0.0f;
+  for (int k = 0; k < splits; ++k) s += partial[static_cast<int64_t>(k) * cols + col];
+  out[col] = s;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -261,11 +307,28 @@ int relu_backward(Context* ctx, const float* g, const float* x, float* out, int6
 int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int rows,
                        cudaStream_t s) {
   if (cols <= 0) return kOk;
-  if (nparray_order(ctx))
+  if (nparray_order(ctx)) {
     reduce_leading_seq_kernel<<<(cols + 127) / 128, 128, 0, s>>>(in, out, cols, rows);
-  else
+    note_launches(1);
+    return cuda_status(cudaGetLastError());
+  }
+  const bool vec = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 15u) == 0;
+  const int col_blocks = (cols + 127) / 128;
+  int splits = std::min((4 * ctx->num_sms + col_blocks - 1) / col_blocks, rows / 64);
+  if (!vec || splits < 2) {
     reduce_leading_kernel<<<(cols + 31) / 32, 256, 0, s>>>(in, out, cols, rows);
-  note_launches(1);
+    note_launches(1);
+    return cuda_status(cudaGetLastError());
+  }
+  splits = std::min(splits, 64);
+  int rc = ensure_small_scratch(ctx, static_cast<size_t>(splits) * cols * sizeof(float));
+  if (rc != kOk) return rc;
+  float* partial = static_cast<float*>(ctx->small_scratch);
+  const int rows_per = (rows + splits - 1) / splits;
+  reduce_leading_part_kernel<<<dim3(col_blocks, splits), 256, 0, s>>>(in, partial, cols, rows,
+                                                                       rows_per);
+  reduce_leading_finish_kernel<<<(cols + 255) / 256, 256, 0, s>>>(partial, out, cols, splits);
+  note_launches(2);
   return cuda_status(cudaGetLastError());
 }
 

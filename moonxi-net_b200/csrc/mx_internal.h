@@ -18,6 +18,7 @@ struct Context {
   cudaStream_t stream = nullptr;  // stream used by calls that take none
   int precision = 0;              // MX_PREC_* default for calls that take none
   int* status = nullptr;          // device words: [0] status code, [1] call site
+  int* sched = nullptr;           // device word: dynamic tile counter (status + 2)
   void* workspace = nullptr;      // scratch for split operands / split-K partials
   size_t ws_bytes = 0;
   void* small_scratch = nullptr;  // reduction partials (loss, gradient norm)
@@ -70,7 +71,17 @@ struct TcLaunch {
   int num_sms;
   int* status;
   uint64_t timeout_ns;
+  // scratch for stream-K partial tiles and counters (tc_streamk_bytes); when
+  // too small the GEMM runs data-parallel over whole tiles
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  // device int for dynamic whole-tile scheduling (zeroed per launch on the
+  // launch stream), or null for a static tile order
+  int* sched = nullptr;
 };
+// Scratch a stream-K launch of this shape needs (0: whole tiles already
+// fill the machine, no stream-K).
+size_t tc_streamk_bytes(int M, int N, int K, int num_sms);
 // One operand in hi/lo split form (lo may be null for passes = 1).
 // kmajor: element (r, k) at hi[r * ld + k]; else at hi[k * ld + r].
 struct SplitOperand {

@@ -157,6 +157,14 @@ class MLP:
         # optional list; when set, each GEMM of step() appends
         # (algorithmic flops, start event, end event) -- used by the benchmark
         self.gemm_timer = None
+        # optional list; when set, the split-form step appends (phase, event)
+        # at its phase boundaries -- used by the benchmark
+        self.phase_marks = None
+        # the first layer's gradient bucket can be reduced in row chunks as
+        # the chunks are computed; measured on 8 B200s this did not shorten
+        # the exposed tail (the chunked GEMMs lose more than the overlap
+        # gains), so one chunk is the default
+        self.last_bucket_chunks = 1
 
     # ------------------------------------------------------------------ state
     def _wshape(self, i):
@@ -313,6 +321,15 @@ class MLP:
             e1.record()
             timer.append((flops, e0, e1))
 
+        marks = self.phase_marks
+
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
+
+        mark("start")
         xh, xl = hsplit[0]
         ops.split_tf32(x, xh, xl, ctx=ctx)
         # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
@@ -324,9 +341,11 @@ class MLP:
                  b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=d[i] if nt else d[i + 1],
                  b_kmajor=nt, M=B, K=d[i], N=d[i + 1], c=acts[i], c_hi=ch, c_lo=cl,
                  bias=self.b[i], relu=not last)
+        mark("forward")
         gh, gl = gsplit[self.L - 1]
         ops.softmax_ce_labels_split(acts[self.L - 1], labels, gbuf[self.L - 1], gh, gl,
                                     self.loss_slot, G, ctx=ctx)
+        mark("loss")
         works = []
         for i in reversed(range(self.L)):
             fi, fo = d[i], d[i + 1]
@@ -334,13 +353,33 @@ class MLP:
             gh, gl = gsplit[i]
             hh, hl = hsplit[i]
             ops.reduce_sum_leading(g, out=self.gb[i], ctx=ctx)
-            if nt:   # dW[out,in] = dY^T X
-                gemm(2 * B * fi * fo, a_hi=gh, a_lo=gl, lda=fo, a_kmajor=False, b_hi=hh,
-                     b_lo=hl, ldb=fi, b_kmajor=False, M=fo, K=B, N=fi, c=self.gw[i])
-            else:    # dW[in,out] = X^T dY
-                gemm(2 * B * fi * fo, a_hi=hh, a_lo=hl, lda=fi, a_kmajor=False, b_hi=gh,
-                     b_lo=gl, ldb=fo, b_kmajor=False, M=fi, K=B, N=fo, c=self.gw[i])
-            if self.pg is not None:
+            # dW in row chunks; with a process group, the first layer's bucket
+            # (the last one backward produces, nothing left to hide it behind)
+            # is all-reduced chunk by chunk as the chunks are computed
+            Mrows, Ncols = (fo, fi) if nt else (fi, fo)
+            nchunk = self.last_bucket_chunks if (self.pg is not None and i == 0) else 1
+            rows_per = -(-Mrows // nchunk)
+            rows_per = -(-rows_per // 128) * 128
+            bstart, bend = self.layout_.bucket(i)
+            r0 = 0
+            while r0 < Mrows:
+                r1 = min(Mrows, r0 + rows_per)
+                if nt:   # dW[out,in] = dY^T X
+                    gemm(2 * B * (r1 - r0) * Ncols, a_hi=gh.view(-1)[r0:], a_lo=gl.view(-1)[r0:],
+                         lda=fo, a_kmajor=False, b_hi=hh, b_lo=hl, ldb=fi, b_kmajor=False,
+                         M=r1 - r0, K=B, N=fi, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
+                else:    # dW[in,out] = X^T dY
+                    gemm(2 * B * (r1 - r0) * Ncols, a_hi=hh.view(-1)[r0:], a_lo=hl.view(-1)[r0:],
+                         lda=fi, a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo, b_kmajor=False,
+                         M=r1 - r0, K=B, N=fo, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
+                if self.pg is not None and nchunk > 1:
+                    import torch.distributed as dist
+                    lo = bstart if r0 == 0 else _LOSS_SLOTS + self.w_off[i] + r0 * Ncols
+                    hi = bend if r1 == Mrows else _LOSS_SLOTS + self.w_off[i] + r1 * Ncols
+                    works.append(dist.all_reduce(self.grads_buf[lo:hi], group=self.pg,
+                                                 async_op=True))
+                r0 = r1
+            if self.pg is not None and nchunk == 1:
                 import torch.distributed as dist
                 works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
             if i > 0:
@@ -350,13 +389,16 @@ class MLP:
                      b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=fi if nt else fo,
                      b_kmajor=not nt, M=B, K=fo, N=fi, c=gbuf[i - 1], c_hi=ph, c_lo=pl,
                      mask=acts[i - 1], ldm=fi)
+        mark("backward")
         for wk in works:
             wk.wait()
+        mark("allreduce_wait")
         if update:
             ops.sgd_momentum_autoclip_split(self.params, self.grads, self.vels, self.params_hi,
                                             self.params_lo, self.lr, self.momentum,
                                             self.weight_decay, self.max_grad_norm,
                                             norm_out=self.norm, ctx=ctx)
+        mark("update")
         return self.loss_slot
 
     # ------------------------------------------------------------ CUDA graph

@@ -4,7 +4,10 @@ Each rank runs the MLP step on its half of the batch with the loss scaled by
 1/global_batch and all-reduces the per-layer gradient buckets; both replicas
 must end bit-identical, and match a single-GPU run on the whole batch within
 the fp32-class tolerance.  The step is also captured in a CUDA graph with its
-all-reduces and replayed.  Needs two visible GPUs (skipped otherwise).
+all-reduces and replayed.  Two models: MLP 3072->1024->1024->10 (per-call
+3xTF32 GEMMs) and a split-form model whose first-layer bucket is reduced in
+row chunks as the chunks are computed.  Needs two visible GPUs (skipped
+otherwise).
 """
 from __future__ import annotations
 
@@ -21,6 +24,7 @@ import torch.multiprocessing as mp
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
 pytestmark = pytest.mark.gpu
 STEPS = 3
+SPLIT_DIMS = [1024, 512, 256, 128]
 
 
 def _free_port():
@@ -29,23 +33,40 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, outdir, use_graph):
+def _problem(model):
+    import sys
+    sys.path.insert(0, ROOT)
+    from moonxi_net_b200 import synthetic
+    if model == "mlp3072":
+        w, b, x, y = synthetic.mlp_problem("mlp3072", batch=512)
+        return [3072, 1024, 1024, 10], w, b, x, y
+    rng = np.random.default_rng(9)
+    d = SPLIT_DIMS
+    w = [synthetic.kaiming_uniform(rng, d[i], (d[i], d[i + 1])) for i in range(len(d) - 1)]
+    b = [np.zeros(d[i + 1], np.float32) for i in range(len(d) - 1)]
+    x = rng.standard_normal((512, d[0]), dtype=np.float32)
+    y = rng.integers(0, d[-1], 512).astype(np.float32)
+    return d, w, b, x, y
+
+
+def _worker(rank, world, port, outdir, use_graph, model):
     import sys
     sys.path.insert(0, ROOT)
     import torch.distributed as dist
-    from moonxi_net_b200 import nn, synthetic
+    from moonxi_net_b200 import nn
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        w, b, x, y = synthetic.mlp_problem("mlp3072", batch=512)
+        dims, w, b, x, y = _problem(model)
         lo, hi = nn.shard_rows(512, rank, world)
         X = torch.from_numpy(x[lo:hi].copy()).to(dev)
         Y = torch.from_numpy(y[lo:hi].copy()).to(dev)
-        m = nn.MLP([3072, 1024, 1024, 10], w, b, precision="3xtf32",
-                   process_group=dist.group.WORLD)
+        m = nn.MLP(dims, w, b, precision="3xtf32", process_group=dist.group.WORLD)
+        assert m.fused == (model == "split")
+        m.last_bucket_chunks = 4  # exercise the chunked first-layer bucket
         losses = []
         if use_graph:
             losses.append(float(m.step(X, Y, 512).item()))
@@ -64,13 +85,14 @@ def _worker(rank, world, port, outdir, use_graph):
         dist.destroy_process_group()
 
 
-def _run(use_graph):
+def _run(use_graph, model):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
         port = _free_port()
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, use_graph)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, use_graph, model))
+                 for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
@@ -82,14 +104,15 @@ def _run(use_graph):
         return [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
 
 
+@pytest.mark.parametrize("model", ["mlp3072", "split"])
 @pytest.mark.parametrize("use_graph", [False, True])
-def test_dp2_matches_single_gpu(cuda_device, use_graph):
-    from moonxi_net_b200 import nn, synthetic
-    r0, r1 = _run(use_graph)
+def test_dp2_matches_single_gpu(cuda_device, use_graph, model):
+    from moonxi_net_b200 import nn
+    r0, r1 = _run(use_graph, model)
     assert np.array_equal(r0["params"], r1["params"])       # identical replicas
     assert np.array_equal(r0["losses"], r1["losses"])
-    w, b, x, y = synthetic.mlp_problem("mlp3072", batch=512)
-    m = nn.MLP([3072, 1024, 1024, 10], w, b, precision="3xtf32")
+    dims, w, b, x, y = _problem(model)
+    m = nn.MLP(dims, w, b, precision="3xtf32")
     X, Y = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
     losses = [float(m.step(X, Y).item()) for _ in range(STEPS)]
     ref = m.params.cpu().numpy().astype(np.float64)

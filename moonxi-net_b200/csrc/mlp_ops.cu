@@ -230,6 +230,71 @@ __global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict
   }
 }
 
+// float4 forms of the two passes above (same per-element arithmetic), for
+// 16-byte aligned buffers whose length is a multiple of 4: four times fewer
+// memory instructions, so the passes run at HBM speed.
+__global__ void norm_sq4_kernel(const float4* __restrict__ g, int64_t n4,
+                                float* __restrict__ partial) {
+  __shared__ float sh[256];
+  float s = 0.0f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += stride) {
+    const float4 v = __ldg(g + i);
+    s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+    s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+    s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+    s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+  }
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) sh[threadIdx.x] = __fadd_rn(sh[threadIdx.x], sh[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partial[blockIdx.x] = sh[0];
+}
+
+__device__ __forceinline__ void sgd_one(float& p, float g, float& v, float lr, float momentum,
+                                        float wd, float clip) {
+  const float cg = __fmul_rn(g, clip);
+  v = __fadd_rn(__fadd_rn(__fmul_rn(momentum, v), cg), __fmul_rn(wd, p));
+  p = __fsub_rn(p, __fmul_rn(lr, v));
+}
+
+__global__ void sgd_update4_kernel(float4* __restrict__ p, const float4* __restrict__ g,
+                                   float4* __restrict__ v, int64_t n4, float lr, float momentum,
+                                   float wd, float max_norm, const float* __restrict__ norm,
+                                   float4* __restrict__ p_hi, float4* __restrict__ p_lo) {
+  const float nv = *norm;
+  const float clip = nv > max_norm ? __fdiv_rn(max_norm, nv) : 1.0f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += stride) {
+    float4 pp = p[i], vv = v[i];
+    const float4 gg = __ldg(g + i);
+    sgd_one(pp.x, gg.x, vv.x, lr, momentum, wd, clip);
+    sgd_one(pp.y, gg.y, vv.y, lr, momentum, wd, clip);
+    sgd_one(pp.z, gg.z, vv.z, lr, momentum, wd, clip);
+    sgd_one(pp.w, gg.w, vv.w, lr, momentum, wd, clip);
+    v[i] = vv;
+    p[i] = pp;
+    if (p_hi) {
+      float4 h, l;
+      h.x = __uint_as_float(f32_to_tf32_rna(pp.x));
+      h.y = __uint_as_float(f32_to_tf32_rna(pp.y));
+      h.z = __uint_as_float(f32_to_tf32_rna(pp.z));
+      h.w = __uint_as_float(f32_to_tf32_rna(pp.w));
+      l.x = __uint_as_float(f32_to_tf32_rna(pp.x - h.x));
+      l.y = __uint_as_float(f32_to_tf32_rna(pp.y - h.y));
+      l.z = __uint_as_float(f32_to_tf32_rna(pp.z - h.z));
+      l.w = __uint_as_float(f32_to_tf32_rna(pp.w - h.w));
+      p_hi[i] = h;
+      p_lo[i] = l;
+    }
+  }
+}
+
 // ---- NpArray-order variants (contexts in MX_PREC_NPARRAY mode): the same
 // sequential fp32 loops as the CPU path, so results are bit-identical to it.
 
@@ -375,16 +440,29 @@ int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int6
   if (rc != kOk) return rc;
   float* partial = static_cast<float*>(ctx->small_scratch);
   float* norm = norm_out ? norm_out : partial + blocks;
+  const bool vec4 = n % 4 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                      reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(p_hi) |
+                      reinterpret_cast<uintptr_t>(p_lo)) & 15u) == 0;
   if (nparray_order(ctx)) {
     seq_sum_kernel<<<1, 1, 0, s>>>(g, n, 1.0f, norm, 1);
     note_launches(2);  // seq_sum, sgd_update
   } else {
-    norm_sq_kernel<<<blocks, 256, 0, s>>>(g, n, partial);
+    if (vec4)
+      norm_sq4_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(g), n / 4, partial);
+    else
+      norm_sq_kernel<<<blocks, 256, 0, s>>>(g, n, partial);
     finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, 1.0f, norm, 1);
     note_launches(3);  // norm_sq, finish_sum, sgd_update
   }
-  sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
-                                                              max_norm, norm, p_hi, p_lo);
+  if (vec4)
+    sgd_update4_kernel<<<grid_for(n / 4, ctx->num_sms), 256, 0, s>>>(
+        reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g),
+        reinterpret_cast<float4*>(v), n / 4, lr, momentum, wd, max_norm, norm,
+        reinterpret_cast<float4*>(p_hi), reinterpret_cast<float4*>(p_lo));
+  else
+    sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
+                                                                max_norm, norm, p_hi, p_lo);
   return cuda_status(cudaGetLastError());
 }
 

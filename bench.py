@@ -47,6 +47,11 @@ def flops_per_sample(dims):
 
 
 FLOP_PER_SAMPLE = flops_per_sample(DIMS)
+# dram__bytes_read.sum + dram__bytes_write.sum of one tc_gemm_kernel<3,1,1>
+# launch (dX = dY.W^T, 8192x4096x4096) of the 1-GPU step, from one ncu capture
+# of `bench.py --steps 2 --warmup 3 --skip-cpu --skip-gemm --no-graph`
+# (algorithmic bytes of that launch: 939.5 MB).
+STEP_DX_TRAFFIC_BYTES = 1749.6e6
 
 
 def load_peaks():
@@ -203,6 +208,35 @@ def measure_tf32_peak(torch, dev, n=8192):
         torch.backends.cuda.matmul.allow_tf32 = prev
     del a, b
     return 2.0 * n ** 3 / best / 1e12
+
+
+def measure_cublas_sgemm(torch, dev, n=8192):
+    """cuBLAS true-FP32 SGEMM throughput (TFLOP/s), median of 5 with L2
+    flushed: the vendor library's figure for the exact-fp32 path, reported
+    beside the SIMT kernel's as context (not part of any timed path)."""
+    a = torch.randn((n, n), device=dev)
+    b = torch.randn((n, n), device=dev)
+    c = torch.empty((n, n), device=dev)
+    flush = torch.empty(int(256e6) // 4, device=dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for _ in range(2):
+            torch.matmul(a, b, out=c)
+        times = []
+        for _ in range(5):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / 1e3)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c, flush
+    return 2.0 * n ** 3 / statistics.median(times) / 1e12
 
 
 def gemm_sweep(torch, ops, peaks, dev, sizes=(8192,)):
@@ -394,6 +428,9 @@ def run_ours(args):
             "fp32_simt": round(r["fp32"] / fp32_peak, 3)}
         gemm_bench["peaks_tflops"] = {"tf32_cublas_measured": round(tf32_peak, 1),
                                       "fp32_simt_nominal_at_max_clock": round(fp32_peak, 1)}
+        sgemm = measure_cublas_sgemm(torch, dev)
+        gemm_bench["cublas_sgemm_8192_tflops"] = round(sgemm, 2)
+        gemm_bench["fp32_simt_vs_cublas_sgemm"] = round(r["fp32"] / sgemm, 3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -416,7 +453,11 @@ def run_ours(args):
                              "per step), no explicit flush"},
             "roofline": {"bound": "tensor", "achieved": round(achieved_tc, 1),
                          "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
-                         "frac": round(achieved_tc / tf32_peak, 4), "traffic": None,
+                         "frac": round(achieved_tc / tf32_peak, 4),
+                         "traffic": STEP_DX_TRAFFIC_BYTES if B == GLOBAL_BATCH else None,
+                         "traffic_note": "DRAM read+write bytes of one dX launch "
+                                         "(8192x4096x4096) from an ncu capture of this "
+                                         "step; algorithmic 939.5 MB",
                          "kernel": "tc_gemm_kernel<3> (tcgen05 kind::tf32, 3 MMAs per "
                                    "multiply-add), TF32 tensor FLOP = 3 x 2MNK",
                          "peak_source": "cuBLAS TF32 GEMM 8192^3 measured in this run (best "

@@ -292,7 +292,8 @@ def run_ours(args):
     w, b, x_all, y_all = synthetic.mlp_problem("wide")
     x_np = np.ascontiguousarray(x_all[rank * B:(rank + 1) * B])
     y_np = np.ascontiguousarray(y_all[rank * B:(rank + 1) * B])
-    model = nn.MLP(DIMS, w, b, layout="nn", precision=args.precision, process_group=pg)
+    model = nn.MLP(DIMS, w, b, layout="nn", precision=args.precision, process_group=pg,
+                   shard_update=args.shard_update)
     del w, b, x_all, y_all
     X = torch.from_numpy(x_np).to(dev)
     Y = torch.from_numpy(y_np).to(dev)
@@ -449,6 +450,9 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "layers": DIMS, "global_batch": GLOBAL_BATCH,
                        "per_gpu_batch": B, "precision": args.precision,
                        "parallelism": f"dp{world}", "cuda_graph": use_graph,
+                       "optimizer_update": "sharded (reduce-scatter / all-gather)"
+                       if model.sharded else ("replicated (all-reduce)" if world > 1
+                                              else "single GPU"),
                        "l2": "inputs larger than L2 (217.8 MB of weights + 128 MB batch "
                              "per step), no explicit flush"},
             "roofline": {"bound": "tensor", "achieved": round(achieved_tc, 1),
@@ -527,6 +531,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32", "auto"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--shard-update", action="store_true",
+                    help="N>1: reduce-scatter the gradients, update 1/N of the parameters "
+                         "per rank, all-gather the weights (default: all-reduce, replicated "
+                         "update)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

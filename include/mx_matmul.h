@@ -245,6 +245,21 @@ int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, const float*
                                        float weight_decay, float max_grad_norm, float* norm_out,
                                        float* p_hi, float* p_lo, void* stream);
 
+/* The two halves of mx_sgd_momentum_autoclip, for a data-parallel update
+ * sharded over ranks (each rank owns some ranges of the flat buffers).  The
+ * reference replicates the whole update on its one device (cuda_kernels.cu
+ * :1884-2029); these let each of G ranks update 1/G of the parameters:
+ *   mx_sum_squares: out[0] = (accumulate ? out[0] : 0) + sum x[i]^2, a fixed
+ *     reduction tree (deterministic); a rank sums its gradient ranges, then
+ *     the ranks all-reduce the partial sums into the squared global norm;
+ *   mx_sgd_momentum_clip: the update of mx_sgd_momentum_autoclip on one
+ *     range, with norm = sqrt(*norm_sq) read on the device. */
+int32_t mx_sum_squares(void* handle, const float* x, int64_t n, float* out, int32_t accumulate,
+                       void* stream);
+int32_t mx_sgd_momentum_clip(void* handle, float* params, const float* grads, float* vels,
+                             int64_t n, float lr, float momentum, float weight_decay,
+                             float max_grad_norm, const float* norm_sq, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,8 @@ SIGNATURES = {
     "mx_softmax_ce_labels": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "mx_sgd_momentum_autoclip": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _vp,
                                         _vp]),
+    "mx_sum_squares": (_i32, [_vp, _vp, _i64, _vp, _i32, _vp]),
+    "mx_sgd_momentum_clip": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _vp, _vp]),
 }
 
 

@@ -543,6 +543,29 @@ MX_EXPORT int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, co
                 s);
 }
 
+MX_EXPORT int32_t mx_sum_squares(void* handle, const float* x, int64_t n, float* out,
+                                 int32_t accumulate, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (n < 0 || !out || (n > 0 && !x)) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c, sum_squares(c, x, n, out, accumulate, s), s);
+}
+
+MX_EXPORT int32_t mx_sgd_momentum_clip(void* handle, float* params, const float* grads,
+                                       float* vels, int64_t n, float lr, float momentum,
+                                       float weight_decay, float max_grad_norm,
+                                       const float* norm_sq, void* stream) {
+  Context* c = resolve(handle);
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (n < 0 || !norm_sq || (n > 0 && (!params || !grads || !vels))) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c,
+                sgd_momentum_clip(c, params, grads, vels, n, lr, momentum, weight_decay,
+                                  max_grad_norm, norm_sq, s),
+                s);
+}
+
 MX_EXPORT int32_t mx_sgd_momentum_autoclip(void* handle, float* params, const float* grads,
                                            float* vels, int64_t n, float lr, float momentum,
                                            float weight_decay, float max_grad_norm,

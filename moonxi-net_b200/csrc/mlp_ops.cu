@@ -174,9 +174,10 @@ __global__ void softmax_ce_kernel(const float* __restrict__ logits,
   }
 }
 
-// Sums n partials in a fixed order with one block; out[0] = sum / denom.
+// Sums n partials in a fixed order with one block, then
+// mode 0: out[0] = sum / denom;  1: out[0] = sqrt(sum);  2: out[0] += sum.
 __global__ void finish_sum_kernel(const float* __restrict__ partial, int n, float denom,
-                                  float* __restrict__ out, int write_sqrt) {
+                                  float* __restrict__ out, int mode) {
   __shared__ float sh[256];
   float s = 0.0f;
   for (int i = threadIdx.x; i < n; i += 256) s = __fadd_rn(s, partial[i]);
@@ -188,7 +189,7 @@ __global__ void finish_sum_kernel(const float* __restrict__ partial, int n, floa
   }
   if (threadIdx.x == 0) {
     const float v = sh[0];
-    out[0] = write_sqrt ? __fsqrt_rn(v) : __fdiv_rn(v, denom);
+    out[0] = mode == 1 ? __fsqrt_rn(v) : mode == 2 ? __fadd_rn(out[0], v) : __fdiv_rn(v, denom);
   }
 }
 
@@ -212,8 +213,9 @@ __global__ void norm_sq_kernel(const float* __restrict__ g, int64_t n, float* __
 __global__ void sgd_update_kernel(float* __restrict__ p, const float* __restrict__ g,
                                   float* __restrict__ v, int64_t n, float lr, float momentum,
                                   float wd, float max_norm, const float* __restrict__ norm,
-                                  float* __restrict__ p_hi, float* __restrict__ p_lo) {
-  const float nv = *norm;
+                                  float* __restrict__ p_hi, float* __restrict__ p_lo,
+                                  int norm_is_sq) {
+  const float nv = norm_is_sq ? __fsqrt_rn(*norm) : *norm;
   const float clip = nv > max_norm ? __fdiv_rn(max_norm, nv) : 1.0f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
@@ -265,8 +267,9 @@ __device__ __forceinline__ void sgd_one(float& p, float g, float& v, float lr, f
 __global__ void sgd_update4_kernel(float4* __restrict__ p, const float4* __restrict__ g,
                                    float4* __restrict__ v, int64_t n4, float lr, float momentum,
                                    float wd, float max_norm, const float* __restrict__ norm,
-                                   float4* __restrict__ p_hi, float4* __restrict__ p_lo) {
-  const float nv = *norm;
+                                   float4* __restrict__ p_hi, float4* __restrict__ p_lo,
+                                   int norm_is_sq) {
+  const float nv = norm_is_sq ? __fsqrt_rn(*norm) : *norm;
   const float clip = nv > max_norm ? __fdiv_rn(max_norm, nv) : 1.0f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
@@ -459,10 +462,51 @@ int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int6
     sgd_update4_kernel<<<grid_for(n / 4, ctx->num_sms), 256, 0, s>>>(
         reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g),
         reinterpret_cast<float4*>(v), n / 4, lr, momentum, wd, max_norm, norm,
-        reinterpret_cast<float4*>(p_hi), reinterpret_cast<float4*>(p_lo));
+        reinterpret_cast<float4*>(p_hi), reinterpret_cast<float4*>(p_lo), 0);
   else
     sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(p, g, v, n, lr, momentum, wd,
-                                                                max_norm, norm, p_hi, p_lo);
+                                                                max_norm, norm, p_hi, p_lo, 0);
+  return cuda_status(cudaGetLastError());
+}
+
+// Pieces of the data-parallel sharded update: the squared norm of one
+// gradient range (accumulated over a rank's ranges, then all-reduced over the
+// ranks by the caller) and the update of one range clipped by that norm.
+int sum_squares(Context* ctx, const float* x, int64_t n, float* out, int accumulate,
+                cudaStream_t s) {
+  if (n <= 0) {
+    if (!accumulate) return cuda_status(cudaMemsetAsync(out, 0, sizeof(float), s));
+    return kOk;
+  }
+  const int blocks = grid_for(n, ctx->num_sms, 4);
+  int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks) * sizeof(float));
+  if (rc != kOk) return rc;
+  float* partial = static_cast<float*>(ctx->small_scratch);
+  if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0)
+    norm_sq4_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x), n / 4, partial);
+  else
+    norm_sq_kernel<<<blocks, 256, 0, s>>>(x, n, partial);
+  finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, 1.0f, out, accumulate ? 2 : 0);
+  note_launches(2);
+  return cuda_status(cudaGetLastError());
+}
+
+int sgd_momentum_clip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
+                      float momentum, float wd, float max_norm, const float* norm_sq,
+                      cudaStream_t s) {
+  if (n <= 0) return kOk;
+  const bool vec4 = n % 4 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                      reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
+  if (vec4)
+    sgd_update4_kernel<<<grid_for(n / 4, ctx->num_sms), 256, 0, s>>>(
+        reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g),
+        reinterpret_cast<float4*>(v), n / 4, lr, momentum, wd, max_norm, norm_sq, nullptr,
+        nullptr, 1);
+  else
+    sgd_update_kernel<<<grid_for(n, ctx->num_sms), 256, 0, s>>>(
+        p, g, v, n, lr, momentum, wd, max_norm, norm_sq, nullptr, nullptr, 1);
+  note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 

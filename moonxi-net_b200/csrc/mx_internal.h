@@ -128,6 +128,13 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
 int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
                           float momentum, float wd, float max_norm, float* norm_out,
                           cudaStream_t s, float* p_hi = nullptr, float* p_lo = nullptr);
+// Data-parallel sharded update: out[0] (+)= sum of x^2 over one range, and
+// the momentum-SGD update of one range clipped by sqrt(*norm_sq).
+int sum_squares(Context* ctx, const float* x, int64_t n, float* out, int accumulate,
+                cudaStream_t s);
+int sgd_momentum_clip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
+                      float momentum, float wd, float max_norm, const float* norm_sq,
+                      cudaStream_t s);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

@@ -47,23 +47,29 @@ class FlatLayout:
     (MLP::params, moonxi-net/model/mlp.mbt:27-29); each block starts on a
     256-byte boundary (zero padding between blocks).  The gradient buffer is
     prefixed by a 64-float slot that carries the step's loss, so that the
-    loss rides in the first layer's all-reduce bucket.  Device-independent:
-    the data-parallel host logic is tested with it on CPU ranks.
+    loss rides in the first layer's all-reduce bucket.  With shard_world = G
+    > 1 every bucket is padded (zeros after its bias) to a multiple of G x 64
+    floats, so it splits into G equal 256-byte aligned pieces (ShardPlan).
+    Device-independent: the data-parallel host logic is tested with it on CPU
+    ranks.
     """
 
-    def __init__(self, dims):
+    def __init__(self, dims, shard_world: int = 1):
         self.dims = list(dims)
         self.L = len(dims) - 1
+        self.shard_world = int(shard_world)
         self.w_off, self.b_off = [], []
-        off = 0
+        # offsets in gradient-buffer coordinates (loss slot first), then shifted
+        cur = _LOSS_SLOTS
         for i in range(self.L):
             fi, fo = self.dims[i], self.dims[i + 1]
-            self.w_off.append(off)
-            off += _round_up(fi * fo)
-            self.b_off.append(off)
-            off += _round_up(fo)
-        self.n_flat = off
-        self.grads_buf_len = _LOSS_SLOTS + off
+            self.w_off.append(cur - _LOSS_SLOTS)
+            cur += _round_up(fi * fo)
+            self.b_off.append(cur - _LOSS_SLOTS)
+            cur += _round_up(fo)
+            cur = _round_up(cur, _ALIGN * self.shard_world)  # bucket boundary
+        self.n_flat = cur - _LOSS_SLOTS
+        self.grads_buf_len = cur
 
     def w_range(self, i):
         return self.w_off[i], self.w_off[i] + self.dims[i] * self.dims[i + 1]
@@ -81,6 +87,52 @@ class FlatLayout:
     def reduce_order(self):
         """Buckets in the order backward produces them (last layer first)."""
         return list(reversed(range(self.L)))
+
+
+class ShardPlan:
+    """Partition of the flat buffers for a data-parallel update sharded over
+    `world` ranks.  Coordinates are those of the gradient buffer (the loss
+    slot first); the parameter, velocity and split-copy buffers carry the same
+    front slot so one range means the same parameters in all of them.  Each
+    layer's bucket splits into `world` equal contiguous pieces; rank r
+    reduce-scatters into, owns and updates piece r of every bucket, and
+    all-gathers the others' pieces of the new weights.  The reduce-scatter
+    and the all-gather are in place (the rank's piece is a view of the
+    bucket), which NCCL and gloo both accept."""
+
+    def __init__(self, layout: FlatLayout, world: int, rank: int):
+        if layout.shard_world != world:
+            raise ValueError("layout was not padded for this world size")
+        self.layout, self.world, self.rank = layout, world, rank
+        self.buckets = [layout.bucket(i) for i in range(layout.L)]
+        self.pieces = []
+        for s, e in self.buckets:
+            per = (e - s) // world
+            assert per * world == e - s and per % _ALIGN == 0
+            self.pieces.append((s + rank * per, s + (rank + 1) * per))
+
+    def update_ranges(self):
+        """This rank's parameter ranges (its pieces minus the loss slot)."""
+        out = []
+        for a, b in self.pieces:
+            a = max(a, _LOSS_SLOTS)
+            if b > a:
+                out.append((a, b))
+        return out
+
+    def reduce_scatter(self, buf, i, group, async_op=True):
+        """Sums bucket i of `buf` over the ranks into this rank's piece."""
+        import torch.distributed as dist
+        s, e = self.buckets[i]
+        a, b = self.pieces[i]
+        return dist.reduce_scatter_tensor(buf[a:b], buf[s:e], group=group, async_op=async_op)
+
+    def all_gather(self, buf, i, group, async_op=True):
+        """Fills bucket i of `buf` with every rank's piece."""
+        import torch.distributed as dist
+        s, e = self.buckets[i]
+        a, b = self.pieces[i]
+        return dist.all_gather_into_tensor(buf[s:e], buf[a:b], group=group, async_op=async_op)
 
 
 def shard_rows(global_batch: int, rank: int, world: int):
@@ -101,7 +153,7 @@ class MLP:
     def __init__(self, dims, weights=None, biases=None, layout: str = "nn", device=None,
                  precision="default", lr: float = 0.01, momentum: float = 0.9,
                  weight_decay: float = 1e-4, max_grad_norm: float = 35.0,
-                 process_group=None, fused=None):
+                 process_group=None, fused=None, shard_update=None):
         if layout not in ("nn", "nt"):
             raise ValueError("layout must be 'nn' (w [in,out]) or 'nt' (w [out,in])")
         self.dims = list(dims)
@@ -116,38 +168,61 @@ class MLP:
         self.lr, self.momentum = float(lr), float(momentum)
         self.weight_decay, self.max_grad_norm = float(weight_decay), float(max_grad_norm)
         self.pg = process_group
+        self.rank = 0
         if process_group is not None:
             import torch.distributed as dist
             self.world = dist.get_world_size(process_group)
+            self.rank = dist.get_rank(process_group)
         else:
             self.world = 1
+        # Split-form path (3xTF32 with every operand kept as hi/lo copies written
+        # by its producer): needs TMA-legal leading dimensions (multiples of 4).
+        self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
+                      and fused is not False)
+        # Sharded update (opt-in; split-form path, several ranks): gradients
+        # are reduce-scattered instead of all-reduced, each rank updates its
+        # 1/G of the parameters, and the new weights are all-gathered layer by
+        # layer at the start of the next step, overlapping its forward, where
+        # each rank re-splits them.  Measured on 2 B200s (wide MLP) it is
+        # slower than the replicated update (1.34 vs 1.38 M samples/s: the
+        # update halves, the forward grows by the gather and the re-split),
+        # so the default stays all-reduce + replicated update.
+        self.sharded = self.fused and self.world > 1 and bool(shard_update)
 
-        self.layout_ = FlatLayout(self.dims)
+        self.layout_ = FlatLayout(self.dims, self.world if self.sharded else 1)
         self.w_off, self.b_off = self.layout_.w_off, self.layout_.b_off
         self.n_flat = self.layout_.n_flat
+        self.plan = ShardPlan(self.layout_, self.world, self.rank) if self.sharded else None
         dev = self.device
-        self.params = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
-        self.vels = torch.zeros(self.n_flat, device=dev, dtype=torch.float32)
+
+        def flat(extra=0):
+            # [front slot (64 floats)] + n_flat (+ extra): every flat buffer shares
+            # the gradient buffer's coordinates, so one range means the same
+            # parameters in all of them (see ShardPlan)
+            return torch.zeros(_LOSS_SLOTS + self.n_flat + extra, device=dev,
+                               dtype=torch.float32)
+        self._params_full, self._vels_full = flat(), flat()
+        self.params = self._params_full[_LOSS_SLOTS:]
+        self.vels = self._vels_full[_LOSS_SLOTS:]
         # grads_buf = [loss slot (64 floats)] + grads (n_flat)
         self.grads_buf = torch.zeros(self.layout_.grads_buf_len, device=dev, dtype=torch.float32)
         self.grads = self.grads_buf[_LOSS_SLOTS:]
         self.loss_slot = self.grads_buf[:1]
+        if self.sharded:
+            # [norm^2 partial -> global, loss partial -> global, zeros]: one small
+            # all-reduce per step after the reduce-scatters
+            self.scalars = torch.zeros(_ALIGN, device=dev, dtype=torch.float32)
+            self.loss_slot = self.scalars[1:2]
         self.norm = torch.zeros(1, device=dev, dtype=torch.float32)
         self.w = [self._view(self.params, i, True) for i in range(self.L)]
         self.b = [self._view(self.params, i, False) for i in range(self.L)]
         self.gw = [self._view(self.grads, i, True) for i in range(self.L)]
         self.gb = [self._view(self.grads, i, False) for i in range(self.L)]
-        # Split-form path (3xTF32 with every operand kept as hi/lo copies written
-        # by its producer): needs TMA-legal leading dimensions (multiples of 4).
-        self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
-                      and fused is not False)
         if self.fused:
             # (+_ALIGN: every split copy keeps readable memory past its last
             # row, so MN-major tiles are fetched as whole 32-wide chunks)
-            self.params_hi = torch.zeros(self.n_flat + _ALIGN, device=dev,
-                                         dtype=torch.float32)[:self.n_flat]
-            self.params_lo = torch.zeros(self.n_flat + _ALIGN, device=dev,
-                                         dtype=torch.float32)[:self.n_flat]
+            self.params_hi = flat(_ALIGN)[_LOSS_SLOTS:_LOSS_SLOTS + self.n_flat]
+            self.params_lo = flat(_ALIGN)[_LOSS_SLOTS:_LOSS_SLOTS + self.n_flat]
             self.w_hi = [self._view(self.params_hi, i, True) for i in range(self.L)]
             self.w_lo = [self._view(self.params_lo, i, True) for i in range(self.L)]
         if weights is not None:
@@ -197,6 +272,21 @@ class MLP:
             out += [self.gw[i].detach().cpu().numpy().copy(),
                     self.gb[i].detach().cpu().numpy().copy()]
         return out
+
+    def sync_params(self, vels: bool = False):
+        """Sharded update only (a collective: every rank calls it): gathers
+        every rank's pieces of the parameters (and of the velocities when
+        asked) so that each replica holds the full state, e.g. before reading
+        or saving it.  The step itself gathers the weights it needs at its
+        start; between steps a rank's buffers are current only on its own
+        pieces.  No-op otherwise."""
+        if not self.sharded:
+            return
+        bufs = [self._params_full] + ([self._vels_full] if vels else [])
+        works = [self.plan.all_gather(buf, i, self.pg) for buf in bufs for i in range(self.L)]
+        for wk in works:
+            wk.wait()
+        ops.split_tf32(self.params, self.params_hi, self.params_lo, ctx=self.ctx)
 
     def bucket(self, i):
         """Flat slice of grads_buf holding layer i's (dW, db); bucket 0 also
@@ -330,11 +420,20 @@ class MLP:
                 marks.append((name, ev))
 
         mark("start")
+        plan = self.plan
+        gathers = []
+        if plan is not None:
+            # the new weights: every rank's pieces, layer by layer, on the
+            # collective stream while the forward of the earlier layers runs
+            gathers = [plan.all_gather(self._params_full, i, self.pg) for i in range(self.L)]
         xh, xl = hsplit[0]
         ops.split_tf32(x, xh, xl, ctx=ctx)
         # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
         for i in range(self.L):
             last = i + 1 == self.L
+            if plan is not None:
+                gathers[i].wait()
+                ops.split_tf32(self.w[i], self.w_hi[i], self.w_lo[i], ctx=ctx)
             ah, al = hsplit[i]
             ch, cl = (None, None) if last else hsplit[i + 1]
             gemm(2 * B * d[i] * d[i + 1], a_hi=ah, a_lo=al, lda=d[i], a_kmajor=True,
@@ -357,7 +456,8 @@ class MLP:
             # (the last one backward produces, nothing left to hide it behind)
             # is all-reduced chunk by chunk as the chunks are computed
             Mrows, Ncols = (fo, fi) if nt else (fi, fo)
-            nchunk = self.last_bucket_chunks if (self.pg is not None and i == 0) else 1
+            nchunk = (self.last_bucket_chunks
+                      if (self.pg is not None and plan is None and i == 0) else 1)
             rows_per = -(-Mrows // nchunk)
             rows_per = -(-rows_per // 128) * 128
             bstart, bend = self.layout_.bucket(i)
@@ -379,7 +479,9 @@ class MLP:
                     works.append(dist.all_reduce(self.grads_buf[lo:hi], group=self.pg,
                                                  async_op=True))
                 r0 = r1
-            if self.pg is not None and nchunk == 1:
+            if plan is not None:
+                works.append(plan.reduce_scatter(self.grads_buf, i, self.pg))
+            elif self.pg is not None and nchunk == 1:
                 import torch.distributed as dist
                 works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
             if i > 0:
@@ -393,13 +495,36 @@ class MLP:
         for wk in works:
             wk.wait()
         mark("allreduce_wait")
-        if update:
+        if plan is not None:
+            self._sharded_update(update)
+        elif update:
             ops.sgd_momentum_autoclip_split(self.params, self.grads, self.vels, self.params_hi,
                                             self.params_lo, self.lr, self.momentum,
                                             self.weight_decay, self.max_grad_norm,
                                             norm_out=self.norm, ctx=ctx)
         mark("update")
         return self.loss_slot
+
+    def _sharded_update(self, update):
+        """Global norm from every rank's gradient pieces (one small
+        all-reduce that also sums the loss), then the update of this rank's
+        pieces.  The new split copies are made after the next step's
+        all-gather, so the update writes p and v only."""
+        import torch.distributed as dist
+        ranges = self.plan.update_ranges()
+        sc = self.scalars
+        if ranges:
+            for k, (a, b) in enumerate(ranges):
+                ops.sum_squares(self.grads_buf[a:b], sc[0:1], accumulate=k > 0, ctx=self.ctx)
+        else:
+            ops.sum_squares(self.grads_buf[:0], sc[0:1], ctx=self.ctx)
+        dist.all_reduce(sc, group=self.pg)
+        if update:
+            for a, b in ranges:
+                ops.sgd_momentum_clip(self._params_full[a:b], self.grads_buf[a:b],
+                                      self._vels_full[a:b], self.lr, self.momentum,
+                                      self.weight_decay, self.max_grad_norm, sc[0:1],
+                                      ctx=self.ctx)
 
     # ------------------------------------------------------------ CUDA graph
     def capture(self, x: torch.Tensor, labels: torch.Tensor, global_batch: int | None = None):

@@ -233,6 +233,25 @@ def sgd_momentum_autoclip_split(params, grads, vels, p_hi, p_lo, lr, momentum, w
     check(rc, "mx_sgd_momentum_autoclip_split")
 
 
+def sum_squares(x, out, accumulate: bool = False, ctx=None, stream=None) -> None:
+    """out[0] = (out[0] if accumulate else 0) + sum(x**2) (mx_sum_squares)."""
+    rc = _lib.lib().mx_sum_squares(_handle(ctx, out), _ptr(x), x.numel(), out.data_ptr(),
+                                   int(accumulate), _stream_ptr(stream))
+    check(rc, "mx_sum_squares")
+
+
+def sgd_momentum_clip(params, grads, vels, lr, momentum, weight_decay, max_grad_norm, norm_sq,
+                      ctx=None, stream=None) -> None:
+    """Momentum-SGD update of one range clipped by sqrt(norm_sq[0])
+    (mx_sgd_momentum_clip)."""
+    n = params.numel()
+    rc = _lib.lib().mx_sgd_momentum_clip(
+        _handle(ctx, params), params.data_ptr(), grads.data_ptr(), vels.data_ptr(), n,
+        float(lr), float(momentum), float(weight_decay), float(max_grad_norm),
+        norm_sq.data_ptr(), _stream_ptr(stream))
+    check(rc, "mx_sgd_momentum_clip")
+
+
 def status(device: int | None = None) -> tuple[int, int]:
     """(status, call site) of the device status word; synchronises, clears it."""
     where = ctypes.c_int32(0)

@@ -4,10 +4,12 @@ Each rank runs the MLP step on its half of the batch with the loss scaled by
 1/global_batch and all-reduces the per-layer gradient buckets; both replicas
 must end bit-identical, and match a single-GPU run on the whole batch within
 the fp32-class tolerance.  The step is also captured in a CUDA graph with its
-all-reduces and replayed.  Two models: MLP 3072->1024->1024->10 (per-call
-3xTF32 GEMMs) and a split-form model whose first-layer bucket is reduced in
-row chunks as the chunks are computed.  Needs two visible GPUs (skipped
-otherwise).
+all-reduces and replayed.  Three models: MLP 3072->1024->1024->10 (per-call
+3xTF32 GEMMs, bucket all-reduce), a split-form model with the sharded update
+(bucket reduce-scatter, each rank updates half the parameters, all-gather of
+the new weights at the next step's start), and the same split-form model
+with bucket all-reduces, its first-layer bucket reduced in row chunks as the
+chunks are computed.  Needs two visible GPUs (skipped otherwise).
 """
 from __future__ import annotations
 
@@ -49,6 +51,13 @@ def _problem(model):
     return d, w, b, x, y
 
 
+def _flat_params(m):
+    """Every weight and bias, concatenated (layout padding excluded: the
+    sharded model pads its buckets to split evenly over the ranks)."""
+    ws, bs = m.weights_numpy()
+    return np.concatenate([a.ravel() for a in ws] + [a.ravel() for a in bs])
+
+
 def _worker(rank, world, port, outdir, use_graph, model):
     import sys
     sys.path.insert(0, ROOT)
@@ -64,8 +73,10 @@ def _worker(rank, world, port, outdir, use_graph, model):
         lo, hi = nn.shard_rows(512, rank, world)
         X = torch.from_numpy(x[lo:hi].copy()).to(dev)
         Y = torch.from_numpy(y[lo:hi].copy()).to(dev)
-        m = nn.MLP(dims, w, b, precision="3xtf32", process_group=dist.group.WORLD)
-        assert m.fused == (model == "split")
+        m = nn.MLP(dims, w, b, precision="3xtf32", process_group=dist.group.WORLD,
+                   shard_update=(model != "split_allreduce"))
+        assert m.fused == (model != "mlp3072")
+        assert m.sharded == (model == "split")
         m.last_bucket_chunks = 4  # exercise the chunked first-layer bucket
         losses = []
         if use_graph:
@@ -77,8 +88,9 @@ def _worker(rank, world, port, outdir, use_graph, model):
         else:
             for _ in range(STEPS):
                 losses.append(float(m.step(X, Y, 512).item()))
+        m.sync_params()  # sharded update: gather every rank's pieces
         torch.cuda.synchronize()
-        np.savez(os.path.join(outdir, f"rank{rank}.npz"), params=m.params.cpu().numpy(),
+        np.savez(os.path.join(outdir, f"rank{rank}.npz"), params=_flat_params(m),
                  losses=np.array(losses))
         dist.barrier()
     finally:
@@ -104,7 +116,7 @@ def _run(use_graph, model):
         return [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
 
 
-@pytest.mark.parametrize("model", ["mlp3072", "split"])
+@pytest.mark.parametrize("model", ["mlp3072", "split", "split_allreduce"])
 @pytest.mark.parametrize("use_graph", [False, True])
 def test_dp2_matches_single_gpu(cuda_device, use_graph, model):
     from moonxi_net_b200 import nn
@@ -115,7 +127,7 @@ def test_dp2_matches_single_gpu(cuda_device, use_graph, model):
     m = nn.MLP(dims, w, b, precision="3xtf32")
     X, Y = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
     losses = [float(m.step(X, Y).item()) for _ in range(STEPS)]
-    ref = m.params.cpu().numpy().astype(np.float64)
+    ref = _flat_params(m).astype(np.float64)
     got = r0["params"].astype(np.float64)
     assert np.linalg.norm(got - ref) <= 1e-5 * np.linalg.norm(ref)
     assert np.allclose(r0["losses"], losses, rtol=0, atol=1e-5)

@@ -346,37 +346,18 @@ def run_ours(args):
     value = GLOBAL_BATCH * args.steps / elapsed
 
     # ---- e2e: every step copies its batch from pinned host memory and reads
-    # the loss back.  As a training loop does, the next batch is uploaded on a
-    # copy stream while the current step runs (two input buffers, one
-    # captured step per buffer); the timed region holds every copy and read.
-    loss_host = []
-    Xb, Yb = [X, torch.empty_like(X)], [Y, torch.empty_like(Y)]
+    # the loss back, through the library's HostBatchPipeline: the next batch
+    # is uploaded on a copy stream while the current step runs (two input
+    # buffers, one captured step per buffer); the timed region holds every
+    # copy and read.
     if use_graph:
-        graphs = [model._graph, model.capture(Xb[1], Yb[1], GLOBAL_BATCH)]
-        steps_fn = [graphs[0].replay, graphs[1].replay]
-    else:
-        steps_fn = [lambda: model.step(Xb[0], Yb[0], GLOBAL_BATCH),
-                    lambda: model.step(Xb[1], Yb[1], GLOBAL_BATCH)]
-    copy_stream = torch.cuda.Stream()
-    ready = [torch.cuda.Event(), torch.cuda.Event()]
+        model.release_graph()
+    pipe = nn.HostBatchPipeline(model, B, GLOBAL_BATCH, use_graph=use_graph)
     barrier()
     e2 = torch.cuda.Event(enable_timing=True)
     e3 = torch.cuda.Event(enable_timing=True)
     e2.record()
-    with torch.cuda.stream(copy_stream):
-        Xb[0].copy_(x_pin, non_blocking=True)
-        Yb[0].copy_(y_pin, non_blocking=True)
-        ready[0].record()
-    for i in range(args.steps):
-        cur, nxt = i % 2, 1 - i % 2
-        if i + 1 < args.steps:  # buffer nxt was last read by step i-1, already done
-            with torch.cuda.stream(copy_stream):
-                Xb[nxt].copy_(x_pin, non_blocking=True)
-                Yb[nxt].copy_(y_pin, non_blocking=True)
-                ready[nxt].record()
-        torch.cuda.current_stream().wait_event(ready[cur])
-        steps_fn[cur]()
-        loss_host.append(float(model.loss_slot.item()))
+    loss_host = pipe.run([(x_pin, y_pin)] * args.steps)
     e3.record()
     barrier()
     e2e_t = torch.tensor([e2.elapsed_time(e3) / 1e3], device=dev)
@@ -384,10 +365,8 @@ def run_ours(args):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = GLOBAL_BATCH * args.steps / float(e2e_t.item())
     h2d = x_pin.numel() * 4 + y_pin.numel() * 4
-    if use_graph:  # graphs holding NCCL calls go before the process group does
-        model.release_graph()
-        del graphs
-    del steps_fn
+    pipe.release()  # graphs holding NCCL calls go before the process group does
+    del pipe
 
     # ---- GEMM time inside one eager step (roofline of the dominant kernel)
     gemm_log = []

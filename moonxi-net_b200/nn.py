@@ -544,3 +544,71 @@ class MLP:
 
     def release_graph(self):
         self._graph = None
+
+
+class HostBatchPipeline:
+    """Trains an MLP from batches in pinned host memory: while one step runs,
+    the next batch is copied to the device on a separate stream, into the
+    other of two device buffers (with CUDA graphs, one captured step per
+    buffer); each step's loss is read back to the host.  This replaces the
+    reference's synchronous upload (`GpuTensor::from_host`,
+    moonxi-net-gpu/tensor/gpu_tensor.mbt:192-211, driven by the data loader
+    moonxi-net/datasets/mnist/mnist.mbt:167-183) with copies that overlap the
+    previous step.
+
+    Run one eager step of the model first (it sizes every workspace) before
+    building the pipeline with `use_graph=True`.  A batch's host memory must
+    stay unchanged until `run` returns.
+    """
+
+    def __init__(self, model: MLP, rows: int, global_batch: int | None = None,
+                 use_graph: bool = True):
+        dev = model.device
+        self.model = model
+        self.global_batch = global_batch
+        self.x = [torch.empty((rows, model.dims[0]), device=dev, dtype=torch.float32)
+                  for _ in range(2)]
+        self.y = [torch.empty(rows, device=dev, dtype=torch.float32) for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(device=dev)
+        self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.graphs = None
+        if use_graph:
+            self.graphs = [model.capture(self.x[i], self.y[i], global_batch) for i in range(2)]
+
+    def _upload(self, slot, x, y):
+        with torch.cuda.stream(self.copy_stream):
+            self.x[slot].copy_(x, non_blocking=True)
+            self.y[slot].copy_(y, non_blocking=True)
+            self.ready[slot].record(self.copy_stream)
+
+    def run(self, batches) -> list[float]:
+        """One training step per (x, y) host batch; returns the losses."""
+        losses = []
+        it = iter(batches)
+        cur_batch = next(it, None)
+        if cur_batch is None:
+            return losses
+        self._upload(0, *cur_batch)
+        i = 0
+        while cur_batch is not None:
+            cur = i % 2
+            nxt_batch = next(it, None)
+            if nxt_batch is not None:
+                # the other buffer was read by step i-1, which has finished:
+                # its loss was read back below
+                self._upload(1 - cur, *nxt_batch)
+            torch.cuda.current_stream().wait_event(self.ready[cur])
+            if self.graphs is not None:
+                self.graphs[cur].replay()
+            else:
+                self.model.step(self.x[cur], self.y[cur], self.global_batch)
+            losses.append(float(self.model.loss_slot.item()))
+            cur_batch = nxt_batch
+            i += 1
+        return losses
+
+    def release(self):
+        """Drops the captured graphs (before the process group goes, when
+        they hold collectives)."""
+        self.graphs = None
+        self.model.release_graph()

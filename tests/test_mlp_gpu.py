@@ -147,6 +147,30 @@ def test_graph_replay_bit_identical(cuda_device):
     graphed.release_graph()
 
 
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_host_batch_pipeline_matches_eager_steps(cuda_device, use_graph):
+    """Batches fed from pinned host memory through HostBatchPipeline (next
+    upload overlapping the current step, two device buffers) train exactly as
+    eager steps on device-resident copies of the same batches."""
+    dims = [1024, 512, 256, 128]
+    rng = np.random.default_rng(11)
+    w = [synthetic.kaiming_uniform(rng, dims[i], (dims[i], dims[i + 1])) for i in range(3)]
+    b = [np.zeros(dims[i + 1], np.float32) for i in range(3)]
+    batches = [(rng.standard_normal((256, dims[0]), dtype=np.float32),
+                rng.integers(0, dims[-1], 256).astype(np.float32)) for _ in range(4)]
+    ref = nn.MLP(dims, w, b, precision="3xtf32")
+    ref_losses = [float(ref.step(_to_dev(x), _to_dev(y)).item()) for x, y in batches]
+    m = nn.MLP(dims, w, b, precision="3xtf32")
+    m.step(_to_dev(batches[0][0]), _to_dev(batches[0][1]), update=False)  # sizes workspaces
+    pipe = nn.HostBatchPipeline(m, 256, use_graph=use_graph)
+    pinned = [(torch.from_numpy(x).pin_memory(), torch.from_numpy(y).pin_memory())
+              for x, y in batches]
+    losses = pipe.run(pinned)
+    pipe.release()
+    assert losses == ref_losses
+    assert torch.equal(m.params, ref.params)
+
+
 def test_wide_mlp_small_batch_matches_oracle(cuda_device):
     """The bench architecture (4096^3 -> 1000) on 64 rows against the oracle."""
     w, b, x, y = synthetic.mlp_problem("wide", batch=64)

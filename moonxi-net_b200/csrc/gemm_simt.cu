@@ -3,6 +3,10 @@
 // Replaces the true-FP32 cublasGemmEx call of the reference's cuda_matmul
 // (moonxi-net-gpu/cuda/cuda_kernels.cu:1464-1499, CUBLAS_COMPUTE_32F).
 //
+// Two kernels.  Grids whose 128 x 256 tiles fill the SMs' waves run the
+// warp-specialised simt_ws_kernel (8 x 16 outputs a thread, described at its
+// definition).  Everything else runs simt_gemm_kernel:
+//
 // Tile: 128 x 128 outputs per CTA, k-blocks of 16, 256 threads, 8 x 8 outputs
 // per thread, 4-stage shared-memory pipeline, two CTAs resident per SM
 // (<= 128 registers a thread, ~97 KB shared memory a CTA) so one CTA's

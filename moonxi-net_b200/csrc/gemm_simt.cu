@@ -39,7 +39,6 @@
 // C's columns allow.
 #include <algorithm>
 #include <cstdio>
-#include <cstdlib>
 
 #include "mx_internal.h"
 #include "mx_ptx.cuh"
@@ -50,12 +49,11 @@ namespace {
 constexpr int kBM = 128, kBK = 16, kThreads = 256;
 constexpr int kTileA = kBM * kBK;  // 2048 floats = 8 KB
 
-// Tile shapes of the block-synchronous kernel, 128 x BN outputs per CTA:
-//   BN = 128: 8 x 8 outputs a thread, 4 landing stages, ~97 KB of shared
-//             memory and <= 128 registers, two CTAs per SM;
-//   BN = 256: 8 x 16 outputs a thread, 5 landing stages, one CTA per SM
-//             (only the cp.async fallback of large grids; their TMA path is
-//             the warp-specialised kernel below).
+// Tile shapes, 128 x BN outputs per CTA:
+//   BN = 128: simt_gemm_kernel, 8 x 8 outputs a thread, 4 landing stages,
+//             ~97 KB of shared memory and <= 128 registers, two CTAs per SM;
+//   BN = 256: simt_ws_kernel's tile, 8 x 16 outputs a thread (its epilogue
+//             uses kGroups; its pipeline has its own constants).
 template <int BN>
 struct Shape {
   static constexpr int kTileB = BN * kBK;
@@ -659,12 +657,7 @@ cudaError_t launch_ws(bool ak, bool bkc, const CUtensorMap& ta, const CUtensorMa
 // with full waves, while in a part-filled last wave the lone 128-wide CTA on
 // an SM runs faster than it did beside a second one, so it loses less.
 int tile_width(const Context* ctx, const GemmArgs& g) {
-  static const int forced = [] {
-    const char* e = std::getenv("MX_SIMT_BN");
-    return e ? std::atoi(e) : 0;
-  }();
   if (g.strict || !tma_ok(g)) return 128;
-  if (forced == 128 || forced == 256) return forced;
   const int64_t wide_tiles =
       static_cast<int64_t>((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256);
   const int64_t waves = (wide_tiles + ctx->num_sms - 1) / ctx->num_sms;
@@ -725,7 +718,7 @@ int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scr
             (p.splits > 1 || (aligned16(g.c) && g.ldc % 4 == 0 &&
                               (g.bias == nullptr || aligned16(g.bias))));
   const bool ak = (g.ta == 0), bkc = (g.tb != 0);
-  const int bn = tile_width(ctx, g);
+  int bn = tile_width(ctx, g);
   const bool tma = tma_ok(g);
   CUtensorMap ta{}, tb{};
   bool use_tma = tma;
@@ -742,15 +735,11 @@ int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scr
     else
       use_tma &= make_tmap_2d(&tb, g.b, g.N, g.K, g.ldb * 4, bn, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
   }
+  if (!use_tma) bn = 128;  // a tensor map was refused: cp.async, 128-wide tiles
   dim3 grid((g.N + bn - 1) / bn, (g.M + kBM - 1) / kBM, p.splits);
   if (grid.y > 65535) return kErrUnsupported;
-  cudaError_t e;
-  if (bn == 256 && use_tma && !g.strict)
-    e = launch_ws(ak, bkc, ta, tb, p, grid, s);
-  else if (bn == 256)
-    e = dispatch_all<256>(g.strict, use_tma, ak, bkc, ta, tb, p, grid, s);
-  else
-    e = dispatch_all<128>(g.strict, use_tma, ak, bkc, ta, tb, p, grid, s);
+  cudaError_t e = bn == 256 ? launch_ws(ak, bkc, ta, tb, p, grid, s)
+                            : dispatch_all<128>(g.strict, use_tma, ak, bkc, ta, tb, p, grid, s);
   if (e != cudaSuccess) return cuda_status(e);
   if (p.splits > 1) {
     const int64_t total = static_cast<int64_t>(g.M) * g.N;

@@ -137,6 +137,17 @@ def test_square_large(cuda_device, n, prec):
     assert rel_err(C, c64, scale) <= tol(prec, n)
 
 
+@pytest.mark.parametrize("ta,tb", LAYOUTS)
+def test_fp32_wide_tile_edges(cuda_device, ta, tb):
+    """Exact FP32 on a grid the 128x256 warp-specialised kernel takes (63 x 32
+    tiles fill 97 % of the waves) with partial tiles in M and N, a K tail
+    (K % 16 = 8), alpha, beta, bias and ReLU, every layout."""
+    M, K, N = 7940, 1000, 8004
+    C, c64, scale, _ = run_case(M, K, N, ta, tb, "fp32", seed=3, bias=True, relu=True,
+                                alpha=0.5, beta=0.25)
+    assert rel_err(C, c64, scale) <= tol("fp32", K)
+
+
 @pytest.mark.parametrize("prec", ["fp32", "3xtf32"])
 @pytest.mark.parametrize("ta,tb", LAYOUTS)
 def test_bias_relu_epilogue(cuda_device, ta, tb, prec):

@@ -36,8 +36,6 @@ namespace mx {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 16;  // kBK fp32 = 64-byte K-major rows
-constexpr int kATile = kBM * kBK * 4;           // 8 KB
-constexpr int kBTile = kBN * kBK * 4;           // 16 KB
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 // K-major tile: [rows][16] fp32, 64-byte rows, 64-byte swizzle; 8-row groups
@@ -49,13 +47,24 @@ constexpr uint32_t kSboK = 8 * kBK * 4;         // 512 B
 constexpr uint32_t kSboMN = 4 * 128;            // 512 B
 constexpr uint32_t kK8MN = 8 * 128;             // 1024 B
 constexpr uint32_t kChunkMN = kBK * 128;        // 2048 B
-constexpr uint32_t kLayoutSw64 = 4, kLayoutSw128Base32 = 1;
+constexpr uint32_t kLayoutSw64 = 4, kLayoutSw128Base32 = 1, kLayoutSw128 = 2;
 
-template <int PASSES>
+// k-block depth of a stage.  Plain TF32 with both operands K-major takes 32
+// k per stage (128-byte rows, 128-byte swizzle): one pass of MMAs per stage
+// is short, and twice the depth halves the TMA copies and barrier round trips
+// per MMA.  Everything else: 16.
+template <int PASSES, bool AK, bool BKM>
+__host__ __device__ constexpr int stage_bk() {
+  return (PASSES == 1 && AK && BKM) ? 32 : 16;
+}
+
+template <int PASSES, int BK = kBK>
 struct Cfg {
   static constexpr int kOperandCopies = PASSES == 3 ? 2 : 1;
-  static constexpr int kStageBytes = kOperandCopies * (kATile + kBTile);
-  static constexpr int kStages = PASSES == 3 ? 4 : 8;
+  static constexpr int kATileB = kBM * BK * 4;  // bytes
+  static constexpr int kBTileB = kBN * BK * 4;
+  static constexpr int kStageBytes = kOperandCopies * (kATileB + kBTileB);
+  static constexpr int kStages = PASSES == 3 ? 4 : (BK == 32 ? 4 : 8);
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
 };
 
@@ -337,10 +346,12 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
-// Descriptor of the k8-th 8-deep slice of an operand tile.
-template <bool KMAJOR>
+// Descriptor of the k8-th 8-deep slice of an operand tile (BK-deep stages;
+// K-major rows of BK floats: 8-row groups 8*BK*4 bytes apart).
+template <bool KMAJOR, int BK = kBK>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int k8) {
-  if (KMAJOR) return sdesc_kmajor(saddr + k8 * 32, kSboK, kLayoutSw64);
+  if (KMAJOR)
+    return sdesc_kmajor(saddr + k8 * 32, 8 * BK * 4, BK == 32 ? kLayoutSw128 : kLayoutSw64);
   return sdesc_mnmajor(saddr + k8 * kK8MN, kChunkMN, kSboMN, kLayoutSw128Base32);
 }
 
@@ -349,7 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                    const TcParams p) {
-  using C = Cfg<PASSES>;
+  constexpr int BK = stage_bk<PASSES, AK, BKM>();
+  using C = Cfg<PASSES, BK>;
+  constexpr int kATile = C::kATileB, kBTile = C::kBTileB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -398,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_kb = (p.K + kBK - 1) / kBK;
+  const int num_kb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -424,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bar_arrive_expect_tx(&full[stage], C::kStageBytes);
           armed[stage] = true;
           armed_parity[stage] = phase;
-          const int k0 = kb * kBK;
+          const int k0 = kb * BK;
           load_operand<AK, kBM>(base, &tmAh, &full[stage], k0, tm * kBM, p.a_map3d);
           if (PASSES == 3) {
             load_operand<AK, kBM>(base + kATile, &tmAl, &full[stage], k0, tm * kBM, p.a_map3d);
@@ -483,12 +496,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t s_bh = s_base + (PASSES == 3 ? 2 * kATile : kATile);
           const uint32_t s_bl = s_base + 2 * kATile + kBTile;
 #pragma unroll
-          for (int k8 = 0; k8 < kBK / 8; ++k8) {
-            const uint64_t ah = operand_desc<AK>(s_ah, k8);
-            const uint64_t bh = operand_desc<BKM>(s_bh, k8);
+          for (int k8 = 0; k8 < BK / 8; ++k8) {
+            const uint64_t ah = operand_desc<AK, BK>(s_ah, k8);
+            const uint64_t bh = operand_desc<BKM, BK>(s_bh, k8);
             if (PASSES == 3) {
-              const uint64_t al = operand_desc<AK>(s_al, k8);
-              const uint64_t bl = operand_desc<BKM>(s_bl, k8);
+              const uint64_t al = operand_desc<AK, BK>(s_al, k8);
+              const uint64_t bl = operand_desc<BKM, BK>(s_bl, k8);
               mma_tf32(d_tmem, al, bh, idesc, accumulate);
               mma_tf32(d_tmem, ah, bl, idesc, 1u);
               mma_tf32(d_tmem, ah, bh, idesc, 1u);
@@ -702,16 +715,16 @@ template <int PASSES, bool AK, bool BKM>
 cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                       const CUtensorMap& bl, const TcParams& p, int grid, cudaStream_t s) {
   auto kern = tc_gemm_kernel<PASSES, AK, BKM>;
+  constexpr int kSmem = Cfg<PASSES, stage_bk<PASSES, AK, BKM>()>::kSmem;
   static unsigned configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<PASSES>::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     configured |= 1u << (dev & 31);
   }
-  kern<<<grid, kThreads, Cfg<PASSES>::kSmem, s>>>(ah, al, bh, bl, p);
+  kern<<<grid, kThreads, kSmem, s>>>(ah, al, bh, bl, p);
   note_launches(1);
   return cudaGetLastError();
 }
@@ -727,12 +740,14 @@ cudaError_t launch_tc_major(bool ak, bool bkm, const CUtensorMap& ah, const CUte
 }
 
 // Tensor map of one split copy.  K-major: element (r, k) at base[r*ld + k],
-// box 16 k x rows, 64-byte swizzle.  MN-major: element (r, k) at
-// base[k*ld + r], box 32 mn x 16 k, 128-byte swizzle of 32-byte atoms.
+// box bk k x rows, 64-byte swizzle (bk = 16) or 128-byte swizzle (bk = 32).
+// MN-major: element (r, k) at base[k*ld + r], box 32 mn x 16 k, 128-byte
+// swizzle of 32-byte atoms.
 bool operand_map(CUtensorMap* m, const float* base, bool kmajor, int R, int K, int64_t ld,
-                 int rows_tile, bool padded) {
+                 int rows_tile, bool padded, int bk = kBK) {
   if (kmajor)
-    return make_tmap_2d(m, base, K, R, ld * 4, kBK, rows_tile, CU_TENSOR_MAP_SWIZZLE_64B);
+    return make_tmap_2d(m, base, K, R, ld * 4, bk, rows_tile,
+                        bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   if (R % 32 == 0 || padded) {
     // dims (32 mn, K, ceil(R/32) chunks): one copy brings a whole MN-major
     // tile, in the chunk-after-chunk order the MMA descriptors expect; chunks
@@ -764,8 +779,10 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   if (!A.hi || !B.hi || (passes == 3 && (!A.lo || !B.lo))) return kErrInvalid;
   if (!E.c && !E.c_hi) return kErrInvalid;
   CUtensorMap tah{}, tal{}, tbh{}, tbl{};
-  bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM, A.padded) &&
-            operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN, B.padded);
+  // plain TF32 with both operands K-major runs 32-deep stages (stage_bk)
+  const int bk = (passes == 1 && A.kmajor && B.kmajor) ? 32 : kBK;
+  bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM, A.padded, bk) &&
+            operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN, B.padded, bk);
   if (passes == 3)
     ok = ok && operand_map(&tal, A.lo, A.kmajor, M, K, A.ld, kBM, A.padded) &&
          operand_map(&tbl, B.lo, B.kmajor, N, K, B.ld, kBN, B.padded);

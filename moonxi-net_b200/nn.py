@@ -570,41 +570,58 @@ class HostBatchPipeline:
                   for _ in range(2)]
         self.y = [torch.empty(rows, device=dev, dtype=torch.float32) for _ in range(2)]
         self.copy_stream = torch.cuda.Stream(device=dev)
-        self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.ready = [torch.cuda.Event(), torch.cuda.Event()]   # batch uploaded
+        self.done = [torch.cuda.Event(), torch.cuda.Event()]    # step using the buffer ended
+        self.loss_ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
         self.graphs = None
         if use_graph:
             self.graphs = [model.capture(self.x[i], self.y[i], global_batch) for i in range(2)]
 
-    def _upload(self, slot, x, y):
+    def _upload(self, slot, x, y, after=None):
         with torch.cuda.stream(self.copy_stream):
+            if after is not None:  # the buffer's previous step must be done with it
+                self.copy_stream.wait_event(after)
             self.x[slot].copy_(x, non_blocking=True)
             self.y[slot].copy_(y, non_blocking=True)
             self.ready[slot].record(self.copy_stream)
 
     def run(self, batches) -> list[float]:
-        """One training step per (x, y) host batch; returns the losses."""
+        """One training step per (x, y) host batch; returns the losses.
+
+        Nothing on the host waits for a step before the next one is queued:
+        the upload into a buffer waits on the GPU for the step that last read
+        it, each step's loss is copied to pinned host memory as the step
+        ends, and the host reads step i's loss while step i+1 runs."""
         losses = []
         it = iter(batches)
         cur_batch = next(it, None)
         if cur_batch is None:
             return losses
+        compute = torch.cuda.current_stream()
         self._upload(0, *cur_batch)
-        i = 0
+        i, pending = 0, None
         while cur_batch is not None:
             cur = i % 2
             nxt_batch = next(it, None)
             if nxt_batch is not None:
-                # the other buffer was read by step i-1, which has finished:
-                # its loss was read back below
-                self._upload(1 - cur, *nxt_batch)
-            torch.cuda.current_stream().wait_event(self.ready[cur])
+                self._upload(1 - cur, *nxt_batch, after=self.done[1 - cur] if i >= 1 else None)
+            compute.wait_event(self.ready[cur])
             if self.graphs is not None:
                 self.graphs[cur].replay()
             else:
                 self.model.step(self.x[cur], self.y[cur], self.global_batch)
-            losses.append(float(self.model.loss_slot.item()))
+            self.done[cur].record(compute)
+            self.loss_host[cur:cur + 1].copy_(self.model.loss_slot, non_blocking=True)
+            self.loss_ready[cur].record(compute)
+            if pending is not None:  # step i-1's loss, read while step i runs
+                self.loss_ready[pending].synchronize()
+                losses.append(float(self.loss_host[pending]))
+            pending = cur
             cur_batch = nxt_batch
             i += 1
+        self.loss_ready[pending].synchronize()
+        losses.append(float(self.loss_host[pending]))
         return losses
 
     def release(self):

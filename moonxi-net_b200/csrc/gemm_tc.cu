@@ -46,16 +46,16 @@ constexpr int kTmemCols = 512;
 constexpr uint32_t kSboK = 8 * kBK * 4;         // 512 B
 constexpr uint32_t kSboMN = 4 * 128;            // 512 B
 constexpr uint32_t kK8MN = 8 * 128;             // 1024 B
-constexpr uint32_t kChunkMN = kBK * 128;        // 2048 B
+constexpr uint32_t kChunkMN = kBK * 128;        // 2048 B (BK-deep stages: BK * 128)
 constexpr uint32_t kLayoutSw64 = 4, kLayoutSw128Base32 = 1, kLayoutSw128 = 2;
 
-// k-block depth of a stage.  Plain TF32 with both operands K-major takes 32
-// k per stage (128-byte rows, 128-byte swizzle): one pass of MMAs per stage
-// is short, and twice the depth halves the TMA copies and barrier round trips
-// per MMA.  Everything else: 16.
+// k-block depth of a stage.  Plain TF32 takes 32 k per stage (K-major rows
+// of 128 bytes with the 128-byte swizzle; MN-major chunks of 32 k x 32 mn):
+// one pass of MMAs per stage is short, and twice the depth halves the TMA
+// copies and barrier round trips per MMA.  3xTF32: 16.
 template <int PASSES, bool AK, bool BKM>
 __host__ __device__ constexpr int stage_bk() {
-  return (PASSES == 1 && AK && BKM) ? 32 : 16;
+  return PASSES == 1 ? 32 : 16;
 }
 
 template <int PASSES, int BK = kBK>
@@ -333,7 +333,7 @@ __device__ __forceinline__ void epilogue_bar() {
 // MN-major tiles are 32-wide chunks: one 3-D copy (32 mn x 16 k x chunks)
 // when the operand's row count is a multiple of 32 (map3d), else one 2-D
 // copy per chunk (out-of-range rows then read as zeros).
-template <bool KMAJOR, int ROWS>
+template <bool KMAJOR, int ROWS, int BK = kBK>
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                              int k0, int r0, bool map3d) {
   if (KMAJOR) {
@@ -342,7 +342,7 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
     tma_load_3d(dst, map, bar, 0, k0, r0 / 32);
   } else {
 #pragma unroll
-    for (int c = 0; c < ROWS / 32; ++c) tma_load_2d(dst + c * kChunkMN, map, bar, r0 + 32 * c, k0);
+    for (int c = 0; c < ROWS / 32; ++c) tma_load_2d(dst + c * BK * 128, map, bar, r0 + 32 * c, k0);
   }
 }
 
@@ -352,7 +352,7 @@ template <bool KMAJOR, int BK = kBK>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int k8) {
   if (KMAJOR)
     return sdesc_kmajor(saddr + k8 * 32, 8 * BK * 4, BK == 32 ? kLayoutSw128 : kLayoutSw64);
-  return sdesc_mnmajor(saddr + k8 * kK8MN, kChunkMN, kSboMN, kLayoutSw128Base32);
+  return sdesc_mnmajor(saddr + k8 * kK8MN, BK * 128, kSboMN, kLayoutSw128Base32);
 }
 
 template <int PASSES, bool AK, bool BKM>
@@ -438,15 +438,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           armed[stage] = true;
           armed_parity[stage] = phase;
           const int k0 = kb * BK;
-          load_operand<AK, kBM>(base, &tmAh, &full[stage], k0, tm * kBM, p.a_map3d);
+          load_operand<AK, kBM, BK>(base, &tmAh, &full[stage], k0, tm * kBM, p.a_map3d);
           if (PASSES == 3) {
-            load_operand<AK, kBM>(base + kATile, &tmAl, &full[stage], k0, tm * kBM, p.a_map3d);
-            load_operand<BKM, kBN>(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN,
-                                   p.b_map3d);
-            load_operand<BKM, kBN>(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0, tn * kBN,
-                                   p.b_map3d);
+            load_operand<AK, kBM, BK>(base + kATile, &tmAl, &full[stage], k0, tm * kBM,
+                                      p.a_map3d);
+            load_operand<BKM, kBN, BK>(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN,
+                                       p.b_map3d);
+            load_operand<BKM, kBN, BK>(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0,
+                                       tn * kBN, p.b_map3d);
           } else {
-            load_operand<BKM, kBN>(base + kATile, &tmBh, &full[stage], k0, tn * kBN, p.b_map3d);
+            load_operand<BKM, kBN, BK>(base + kATile, &tmBh, &full[stage], k0, tn * kBN,
+                                       p.b_map3d);
           }
           if (++stage == C::kStages) {
             stage = 0;
@@ -776,7 +778,7 @@ cudaError_t launch_tc_major(bool ak, bool bkm, const CUtensorMap& ah, const CUte
 
 // Tensor map of one split copy.  K-major: element (r, k) at base[r*ld + k],
 // box bk k x rows, 64-byte swizzle (bk = 16) or 128-byte swizzle (bk = 32).
-// MN-major: element (r, k) at base[k*ld + r], box 32 mn x 16 k, 128-byte
+// MN-major: element (r, k) at base[k*ld + r], box 32 mn x bk k, 128-byte
 // swizzle of 32-byte atoms.
 bool operand_map(CUtensorMap* m, const float* base, bool kmajor, int R, int K, int64_t ld,
                  int rows_tile, bool padded, int bk = kBK) {
@@ -791,16 +793,44 @@ bool operand_map(CUtensorMap* m, const float* base, bool kmajor, int R, int K, i
     // rows/columns that are never stored.
     const uint64_t dims[3] = {32, static_cast<uint64_t>(K), static_cast<uint64_t>((R + 31) / 32)};
     const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 4, 128};
-    const uint32_t box[3] = {32, static_cast<uint32_t>(kBK), static_cast<uint32_t>(rows_tile / 32)};
+    const uint32_t box[3] = {32, static_cast<uint32_t>(bk), static_cast<uint32_t>(rows_tile / 32)};
     return make_tmap_3d(m, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   }
-  return make_tmap_2d(m, base, R, K, ld * 4, 32, kBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  return make_tmap_2d(m, base, R, K, ld * 4, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 }  // namespace
 
+namespace {
+// One split copy of an operand, in the layout the operand is stored in (no
+// transpose): K-contiguous -> [rows][Kp] (K-major tiles); MN-contiguous ->
+// [K][rows4], read as MN-major tiles, with 32 floats of slack so that whole
+// 32-wide MN chunks can be fetched.  Kp, rows4: rounded up to 4 (16-byte
+// TMA strides).
+struct CopyShape {
+  bool kmajor;
+  int64_t ld;
+  size_t bytes;
+};
+CopyShape copy_shape(bool kcontig, int rows, int K) {
+  if (kcontig) {
+    const int64_t kp = (static_cast<int64_t>(K) + 3) & ~static_cast<int64_t>(3);
+    return {true, kp, align256(static_cast<size_t>(rows) * kp * 4)};
+  }
+  const int64_t r4 = (static_cast<int64_t>(rows) + 3) & ~static_cast<int64_t>(3);
+  return {false, r4, align256((static_cast<size_t>(K) * r4 + 32) * 4)};
+}
+}  // namespace
+
 // Workspace bytes tc_gemm needs for the split operands of this shape.
 size_t tc_gemm_workspace_bytes(const GemmArgs& g, int passes) {
+  const size_t copies = passes == 3 ? 2 : 1;
+  return copies * (copy_shape(g.ta == 0, g.M, g.K).bytes + copy_shape(g.tb != 0, g.N, g.K).bytes);
+}
+
+// K-major split copies of both operands (the carve-up of the allocation-free
+// entry point below).
+size_t kmajor_split_bytes(const GemmArgs& g, int passes) {
   const size_t kp = (static_cast<size_t>(g.K) + 3) & ~static_cast<size_t>(3);
   const size_t copies = passes == 3 ? 2 : 1;
   return copies * (align256(static_cast<size_t>(g.M) * kp * 4) +
@@ -814,8 +844,8 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   if (!A.hi || !B.hi || (passes == 3 && (!A.lo || !B.lo))) return kErrInvalid;
   if (!E.c && !E.c_hi) return kErrInvalid;
   CUtensorMap tah{}, tal{}, tbh{}, tbl{};
-  // plain TF32 with both operands K-major runs 32-deep stages (stage_bk)
-  const int bk = (passes == 1 && A.kmajor && B.kmajor) ? 32 : kBK;
+  // plain TF32 runs 32-deep stages (stage_bk)
+  const int bk = passes == 1 ? 32 : kBK;
   bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM, A.padded, bk) &&
             operand_map(&tbh, B.hi, B.kmajor, N, K, B.ld, kBN, B.padded, bk);
   if (passes == 3)
@@ -898,32 +928,37 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return kOk;
   if (g.K == 0) return simt_gemm(ctx, g, s);
   if (passes != 1 && passes != 3) return kErrInvalid;
-  const int64_t Kp = (static_cast<int64_t>(g.K) + 3) & ~static_cast<int64_t>(3);
+  const CopyShape ca = copy_shape(g.ta == 0, g.M, g.K), cb = copy_shape(g.tb != 0, g.N, g.K);
   const size_t split_bytes = tc_gemm_workspace_bytes(g, passes);
   const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->num_sms);
   int rc = ensure_workspace(ctx, split_bytes + sk_bytes);
   if (rc != kOk) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);
   float* a_hi = reinterpret_cast<float*>(ws);
-  ws += align256(static_cast<size_t>(g.M) * Kp * 4);
+  ws += ca.bytes;
   float* b_hi = reinterpret_cast<float*>(ws);
-  ws += align256(static_cast<size_t>(g.N) * Kp * 4);
+  ws += cb.bytes;
   float* a_lo = nullptr;
   float* b_lo = nullptr;
   if (passes == 3) {
     a_lo = reinterpret_cast<float*>(ws);
-    ws += align256(static_cast<size_t>(g.M) * Kp * 4);
+    ws += ca.bytes;
     b_lo = reinterpret_cast<float*>(ws);
   }
-  cudaError_t e = launch_split(g.a, g.lda, g.ta == 0, g.M, g.K, Kp, a_hi, a_lo, ctx->num_sms, s);
+  // elementwise split in the stored layout: [rows][K] or [K][rows]
+  cudaError_t e = ca.kmajor
+      ? launch_split(g.a, g.lda, true, g.M, g.K, ca.ld, a_hi, a_lo, ctx->num_sms, s)
+      : launch_split(g.a, g.lda, true, g.K, g.M, ca.ld, a_hi, a_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
-  e = launch_split(g.b, g.ldb, g.tb != 0, g.N, g.K, Kp, b_hi, b_lo, ctx->num_sms, s);
+  e = cb.kmajor ? launch_split(g.b, g.ldb, true, g.N, g.K, cb.ld, b_hi, b_lo, ctx->num_sms, s)
+                : launch_split(g.b, g.ldb, true, g.K, g.N, cb.ld, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
   TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
   L.sched = ctx->sched;
   L.ws = static_cast<uint8_t*>(ctx->workspace) + split_bytes;  // split_bytes is 256-aligned
   L.ws_bytes = sk_bytes;
-  SplitOperand A{a_hi, a_lo, Kp, true}, B{b_hi, b_lo, Kp, true};
+  SplitOperand A{a_hi, a_lo, ca.ld, ca.kmajor, !ca.kmajor},
+      B{b_hi, b_lo, cb.ld, cb.kmajor, !cb.kmajor};
   TcEpilogue E{};
   E.c = g.c; E.ldc = g.ldc; E.alpha = g.alpha; E.beta = g.beta; E.bias = g.bias; E.relu = g.relu;
   return tc_gemm_split(L, A, B, E, g.M, g.N, g.K, passes, s);
@@ -1009,7 +1044,7 @@ extern "C" __attribute__((visibility("default"))) int32_t mx_gemm_3xtf32_noalloc
   g.ldb = g.tb ? K : N;
   g.ldc = N;
   g.alpha = alpha; g.beta = beta; g.bias = bias; g.relu = relu ? 1 : 0;
-  const size_t need = tc_gemm_workspace_bytes(g, 3);
+  const size_t need = kmajor_split_bytes(g, 3);
   if (need > kNoAllocScratchBytes) return kErrUnsupported;  // beyond the static scratch
   NoAllocDevice* d = nullptr;
   int rc = noalloc_setup(&d);

@@ -1059,7 +1059,7 @@ extern "C" __attribute__((visibility("default"))) int32_t mx_gemm_3xtf32_noalloc
     return simt_gemm_launch(&local, g, s, nullptr, 0);
   }
   const int64_t Kp = (static_cast<int64_t>(K) + 3) & ~static_cast<int64_t>(3);
-  uint8_t* ws = d->scratch;  // same carve-up as the workspace of tc_gemm
+  uint8_t* ws = d->scratch;  // K-major copies of both operands (kmajor_split_bytes)
   float* a_hi = reinterpret_cast<float*>(ws);
   ws += align256(static_cast<size_t>(M) * Kp * 4);
   float* b_hi = reinterpret_cast<float*>(ws);

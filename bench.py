@@ -112,60 +112,111 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_rate_sample(target_s: float, dims=DIMS, max_rows: int = 256):
-    """Times the oracle (NpArray restatement, all host threads) on a row
-    sample of the wide-MLP step.  Returns (samples/s, rows, seconds, threads)."""
+def _oracle_model():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # test/baseline infrastructure only
     from moonxi_net_b200 import synthetic
     threads = oracle.default_threads()
     w, b, _, _ = synthetic.mlp_problem("wide", batch=1)
+    return oracle, oracle.MLPOracle(w, b, threads=threads), threads
+
+
+def _rows(rng, n):
+    x = rng.standard_normal((n, DIMS[0]), dtype=np.float32)
+    y = rng.integers(0, DIMS[-1], n).astype(np.float32)
+    return x, y
+
+
+def _fit_full_step(pts):
+    """Least-squares line t = fixed + rows * per_row through (rows, seconds)
+    points of the CPU step; returns (fixed_s, per_row_s, full_step_s) for the
+    global batch.  A step of the NpArray path has a fixed part (the
+    transposed weight copies of every matmul, nparray/trait_impl.mbt:205-249,
+    and the optimizer pass over all 54.4M parameters, :280-311) and a part
+    linear in the rows, so a sample of a few rows must not be divided by its
+    own row count."""
+    r = np.array([p[0] for p in pts], np.float64)
+    t = np.array([p[1] for p in pts], np.float64)
+    per_row, fixed = np.polyfit(r, t, 1)
+    if per_row <= 0:  # noise: fall back to the largest sample's rate
+        k = int(np.argmax(r))
+        per_row, fixed = t[k] / r[k], 0.0
+    fixed = max(0.0, float(fixed))
+    return fixed, float(per_row), fixed + GLOBAL_BATCH * float(per_row)
+
+
+def _calibrate(m, rng):
+    """(fixed_s, per_row_s, points) estimate of the CPU step from 8 and 40
+    rows; the points also enter the final fit."""
+    pts = []
+    for n in (8, 40):
+        x, y = _rows(rng, n)
+        t0 = time.perf_counter()
+        m.step(x, y, denom=GLOBAL_BATCH)
+        pts.append((n, time.perf_counter() - t0))
+    per_row = max((pts[1][1] - pts[0][1]) / 32.0, 1e-4)
+    return max(pts[0][1] - 8 * per_row, 0.0), per_row, pts
+
+
+def _sample_sizes(fixed, per_row, budget_s):
+    """Two row counts for the fit: 16 and the largest multiple of 16 (<= 512)
+    whose step fits `budget_s`."""
+    large = int((budget_s - fixed) / per_row) // 16 * 16
+    return 16, max(64, min(512, large))
+
+
+def cpu_rate_sample(target_s: float):
+    """Times the oracle (NpArray restatement, all host threads) on two row
+    samples of the wide-MLP step and extrapolates the full 8192-row step.
+    Returns the cpu_baseline dict."""
+    oracle, m, threads = _oracle_model()
     rng = np.random.default_rng(3)
-    # calibrate on 8 rows, then size the sample for ~target_s
-    m = oracle.MLPOracle(w, b, threads=threads)
-    x8 = rng.standard_normal((8, dims[0]), dtype=np.float32)
-    y8 = rng.integers(0, dims[-1], 8).astype(np.float32)
-    t0 = time.perf_counter()
-    m.step(x8, y8)
-    t_cal = time.perf_counter() - t0
-    rows = int(max(8, min(max_rows, 8 * target_s / max(t_cal, 1e-3))))
-    rows = max(8, rows // 8 * 8)
-    x = rng.standard_normal((rows, dims[0]), dtype=np.float32)
-    y = rng.integers(0, dims[-1], rows).astype(np.float32)
-    t0 = time.perf_counter()
-    m.step(x, y, denom=GLOBAL_BATCH)
-    dt = time.perf_counter() - t0
-    return rows / dt, rows, dt, threads
+    fixed0, per_row0, pts = _calibrate(m, rng)
+    small, large = _sample_sizes(fixed0, per_row0, max(1.0, target_s / 2 - fixed0))
+    for n in (small, large):
+        x, y = _rows(rng, n)
+        t0 = time.perf_counter()
+        m.step(x, y, denom=GLOBAL_BATCH)
+        pts.append((n, time.perf_counter() - t0))
+    fixed, per_row, full = _fit_full_step(pts)
+    return {"value": GLOBAL_BATCH / full, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"NpArray restatement, one fwd+bwd+SGD step at {small} and {large} rows "
+                      f"({pts[0][1]:.2f} s, {pts[1][1]:.2f} s); fitted fixed {fixed:.2f} s + "
+                      f"{per_row * 1e3:.2f} ms/row, extrapolated to the {GLOBAL_BATCH}-row "
+                      f"step ({full:.1f} s)",
+            "fixed_s": round(fixed, 3), "per_row_ms": round(per_row * 1e3, 3),
+            "full_step_s": round(full, 2)}
 
 
 def run_reference(args):
+    """The reference's CPU algorithm (the NpArray restatement, all host
+    threads) on the same workload.  Each step runs a bounded row sample of
+    the global batch, alternating two sample sizes; the rate is the
+    full-batch step extrapolated from the fitted fixed + per-row cost."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0  # the CPU reference runs once, on rank 0
-    budget_per_step = max(1.0, 90.0 / max(1, args.steps + args.warmup))
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-    from moonxi_net_b200 import synthetic
-    threads = oracle.default_threads()
-    w, b, _, _ = synthetic.mlp_problem("wide", batch=1)
-    m = oracle.MLPOracle(w, b, threads=threads)
+    oracle, m, threads = _oracle_model()
     rng = np.random.default_rng(3)
-    # calibrate rows per step
-    x8 = rng.standard_normal((8, DIMS[0]), dtype=np.float32)
-    y8 = rng.integers(0, DIMS[-1], 8).astype(np.float32)
-    t0 = time.perf_counter()
-    m.step(x8, y8, denom=GLOBAL_BATCH)
-    t_cal = time.perf_counter() - t0
-    rows = int(max(8, min(512, 8 * budget_per_step / max(t_cal, 1e-3)))) // 8 * 8
-    x = rng.standard_normal((rows, DIMS[0]), dtype=np.float32)
-    y = rng.integers(0, DIMS[-1], rows).astype(np.float32)
-    for _ in range(args.warmup):
+    # about 90 s of sampled steps in all (the mean of the two sizes per step)
+    budget_per_step = max(1.0, 90.0 / max(1, args.steps + args.warmup))
+    fixed0, per_row0, cal_pts = _calibrate(m, rng)
+    small, large = _sample_sizes(fixed0, per_row0, 2 * budget_per_step - fixed0 - 16 * per_row0)
+    samples = {small: _rows(rng, small), large: _rows(rng, large)}
+    sizes = [small if i % 2 == 0 else large for i in range(args.steps)]
+    for i in range(args.warmup):
+        x, y = samples[small if i % 2 == 0 else large]
         m.step(x, y, denom=GLOBAL_BATCH)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
+    pts = []
+    t_all = time.perf_counter()
+    for n in sizes:
+        x, y = samples[n]
+        t0 = time.perf_counter()
         m.step(x, y, denom=GLOBAL_BATCH)
-    dt = time.perf_counter() - t0
-    value = rows * args.steps / dt
+        pts.append((n, time.perf_counter() - t0))
+    dt = time.perf_counter() - t_all
+    fixed, per_row, full = _fit_full_step(cal_pts + pts)
+    value = GLOBAL_BATCH / full
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -173,10 +224,17 @@ def run_reference(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) inputs, uniform labels, Kaiming-uniform weights)",
         "config": {"workload": WORKLOAD, "layers": DIMS, "global_batch": GLOBAL_BATCH,
-                   "rows_per_step_sample": rows},
+                   "rows_per_step_samples": [small, large]},
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows of the global batch per step (one fwd+bwd+SGD "
-                                   f"over the full 54.4M-parameter model), {args.steps} steps"},
+                         "sample": f"each timed step is one fwd+bwd+SGD step of the NpArray "
+                                   f"restatement on {small} or {large} rows (alternating; "
+                                   f"with calibration steps at 8 and 40 rows in the fit); "
+                                   f"fitted fixed {fixed:.2f} s + {per_row * 1e3:.2f} ms/row, "
+                                   f"value = {GLOBAL_BATCH} / ({full:.1f} s extrapolated "
+                                   f"{GLOBAL_BATCH}-row step); ms_per_step is the mean "
+                                   f"sampled step",
+                         "fixed_s": round(fixed, 3), "per_row_ms": round(per_row * 1e3, 3),
+                         "full_step_s": round(full, 2)},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -239,6 +297,24 @@ def measure_cublas_sgemm(torch, dev, n=8192):
     return 2.0 * n ** 3 / statistics.median(times) / 1e12
 
 
+def _time_median(torch, fn, flush, reps=5, warm=2):
+    """Median CUDA-event time (s) of fn() on the current stream, L2 flushed
+    (a 256 MB write) before every timed call."""
+    for _ in range(warm):
+        fn()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    return statistics.median(times)
+
+
 def gemm_sweep(torch, ops, peaks, dev, sizes=(8192,)):
     """TFLOP/s of the square NN GEMM per precision (L2 flushed between runs)."""
     out = {}
@@ -249,23 +325,132 @@ def gemm_sweep(torch, ops, peaks, dev, sizes=(8192,)):
         c = torch.empty((n, n), device=dev)
         res = {}
         for prec in ("3xtf32", "tf32", "fp32"):
-            for _ in range(2):
-                ops.gemm(a, b, n, n, n, out=c, precision=prec)
-            times = []
-            for _ in range(5):
-                flush.zero_()
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-                ops.gemm(a, b, n, n, n, out=c, precision=prec)
-                e1.record()
-                torch.cuda.synchronize()
-                times.append(e0.elapsed_time(e1) / 1e3)
-            t = statistics.median(times)
+            t = _time_median(torch, lambda: ops.gemm(a, b, n, n, n, out=c, precision=prec), flush)
             res[prec] = round(2.0 * n ** 3 / t / 1e12, 2)
         out[f"{n}^3_nn_tflops"] = res
         del a, b, c
     return out
+
+
+def square_config_sweep(torch, ops, dev, tf32_peak, fp32_peak):
+    """BASELINE config "Square fp32 GEMM sweep": M=N=K in 512..8192, NN/NT/TN,
+    with and without the bias+ReLU epilogue, N(0,1) entries seed 1, every
+    precision; TFLOP/s (median of 5, L2 flushed) and the fraction of the
+    precision's peak (3xTF32 in TF32-equivalent terms, 3 x 2N^3)."""
+    from moonxi_net_b200 import synthetic
+    flush = torch.empty(int(256e6) // 4, device=dev)
+    rows = {}
+    for n in (512, 1024, 2048, 4096, 8192):
+        for lay, (ta, tb) in (("nn", (0, 0)), ("nt", (0, 1)), ("tn", (1, 0))):
+            a_np, b_np, bias_np = synthetic.gemm_problem(n, n, n, ta, tb, 1, True)
+            a = torch.from_numpy(a_np).to(dev)
+            b = torch.from_numpy(b_np).to(dev)
+            bias = torch.from_numpy(bias_np).to(dev)
+            c = torch.empty((n, n), device=dev)
+            for epi in ("plain", "bias_relu"):
+                bv, relu = (bias, True) if epi == "bias_relu" else (None, False)
+                for prec in ("3xtf32", "tf32", "fp32"):
+                    t = _time_median(torch, lambda: ops.gemm(a, b, n, n, n, ta=ta, tb=tb, bias=bv,
+                                                             relu=relu, out=c, precision=prec),
+                                     flush, reps=5 if n >= 2048 else 9)
+                    tf = 2.0 * n ** 3 / t / 1e12
+                    frac = (3 * tf / tf32_peak if prec == "3xtf32" else
+                            tf / tf32_peak if prec == "tf32" else tf / fp32_peak)
+                    rows[f"{n}_{lay}_{epi}_{prec}"] = [round(tf, 2), round(frac, 3)]
+            del a, b, c, bias
+    return {"unit": "[TFLOP/s, fraction of peak]", "peaks_tflops": {
+        "tf32": round(tf32_peak, 1), "fp32_simt": round(fp32_peak, 1)}, "results": rows}
+
+
+def ragged_config_sweep(torch, ops, dev, hbm_peak, tf32_peak, fp32_peak):
+    """BASELINE config "Ragged/skinny GEMMs": M in {1,7,33,127,1000} x K in
+    {512,784,3072,4096} x N in {10,100,257,1000}, N(0,1) seed 4, NN/NT/TN,
+    bias+ReLU epilogue, the default (AUTO) precision.  M <= 33 is judged on
+    HBM bandwidth (algorithmic bytes 4(MK+KN+MN+N)), the others on TFLOP/s."""
+    from moonxi_net_b200 import synthetic
+    flush = torch.empty(int(256e6) // 4, device=dev)
+    per_m = {}
+    for M in (1, 7, 33, 127, 1000):
+        vals = []
+        for K in (512, 784, 3072, 4096):
+            for N in (10, 100, 257, 1000):
+                for ta, tb in ((0, 0), (0, 1), (1, 0)):
+                    a_np, b_np, bias_np = synthetic.gemm_problem(M, K, N, ta, tb, 4, True)
+                    a = torch.from_numpy(a_np).to(dev)
+                    b = torch.from_numpy(b_np).to(dev)
+                    bias = torch.from_numpy(bias_np).to(dev)
+                    c = torch.empty((M, N), device=dev)
+                    t = _time_median(torch, lambda: ops.gemm(a, b, M, K, N, ta=ta, tb=tb,
+                                                             bias=bias, relu=True, out=c),
+                                     flush, reps=7)
+                    if M <= 33:
+                        vals.append(4.0 * (M * K + K * N + M * N + N) / t / 1e9)
+                    else:
+                        vals.append(2.0 * M * N * K / t / 1e12)
+        vals.sort()
+        if M <= 33:
+            per_m[f"M={M}"] = {"unit": "GB/s", "median": round(statistics.median(vals), 1),
+                               "min": round(vals[0], 1), "max": round(vals[-1], 1),
+                               "median_frac_of_hbm": round(statistics.median(vals) / hbm_peak, 3),
+                               "shapes": len(vals)}
+        else:
+            per_m[f"M={M}"] = {"unit": "TFLOP/s", "median": round(statistics.median(vals), 2),
+                               "min": round(vals[0], 2), "max": round(vals[-1], 2),
+                               "median_frac_of_fp32_simt": round(statistics.median(vals) /
+                                                                 fp32_peak, 3),
+                               "shapes": len(vals)}
+    return {"hbm_peak_gbs": hbm_peak, "precision": "auto (exact FP32 SIMT for these shapes "
+            "unless M, N >= 128 and 2MNK >= 1e9: 3xTF32)", "per_M": per_m}
+
+
+def mlp_config_bench(torch, nn, synthetic, dev, tf32_peak):
+    """BASELINE configs "MLP 3072->1024->1024->10, batch 512, 200 steps"
+    (samples/s over 200 captured steps) and "MLP 784->256->10, batch 64"
+    (latency of one captured step), both 3xTF32 on one GPU."""
+    out = {}
+    for name, dims, batch, steps in (("mlp3072", [3072, 1024, 1024, 10], 512, 200),
+                                     ("mlp784", [784, 256, 10], 64, 200)):
+        w, b, x, y = synthetic.mlp_problem(name, batch=batch)
+        m = nn.MLP(dims, w, b, precision="3xtf32")
+        X, Y = torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)
+        m.step(X, Y)
+        torch.cuda.synchronize()
+        m.capture(X, Y)
+        for _ in range(5):
+            m.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            m.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / steps
+        fl = flops_per_sample(dims) * batch
+        out[name] = {"samples_per_s": round(batch / t, 1), "ms_per_step": round(t * 1e3, 4),
+                     "steps": steps, "batch": batch, "model_tflops": round(fl / t / 1e12, 2),
+                     "frac_of_tf32_peak_3x": round(3 * fl / t / 1e12 / tf32_peak, 3),
+                     "final_loss": float(m.loss_slot.item())}
+        m.close()
+        del m
+    return out
+
+
+def single_gpu_loss(torch, nn, synthetic, dev, n_steps):
+    """Loss after n_steps of the same training on one GPU and the whole
+    global batch: the reference point of a data-parallel run's loss."""
+    w, b, x, y = synthetic.mlp_problem("wide")
+    m = nn.MLP(DIMS, w, b, layout="nn", precision="3xtf32")
+    X, Y = torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)
+    del w, b, x, y
+    for _ in range(n_steps):
+        m.step(X, Y, GLOBAL_BATCH)
+    loss = float(m.loss_slot.item())
+    m.close()
+    del m, X, Y
+    torch.cuda.empty_cache()
+    return loss
 
 
 def run_ours(args):
@@ -388,36 +573,64 @@ def run_ours(args):
     phases = {marks[i][0]: round(marks[i - 1][1].elapsed_time(marks[i][1]), 3)
               for i in range(1, len(marks))}
 
+    # ---- data-parallel correctness, outside every timed region: every
+    # replica must hold bit-identical parameters (element-wise MAX == MIN over
+    # the ranks), and the loss must match one GPU trained the same way
+    dp_check = {}
+    if pg is not None:
+        model.sync_params()
+        pmax = model.params.clone()
+        pmin = model.params.clone()
+        dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(pmin, op=dist.ReduceOp.MIN)
+        dp_check["replicas_identical"] = bool(torch.equal(pmax, pmin))
+        del pmax, pmin
+        # steps so far: 1 eager + W warm-up + K timed + K e2e + 2 instrumented
+        n_done = 1 + args.warmup + 2 * args.steps + 2
+        if rank == 0:
+            dp_loss = float(model.loss_slot.item())
+            ref_loss = single_gpu_loss(torch, nn, synthetic, dev, n_done)
+            dp_check.update({"steps_compared": n_done, "loss_dp": dp_loss, "loss_n1": ref_loss,
+                             "loss_vs_n1": abs(dp_loss - ref_loss)})
+        dist.barrier()
+
+    # Roofline denominator of the TF32 tensor pipe: half the measured dense
+    # bf16 rate of MEASURED_PEAKS.json (B200's TF32 rate is half its bf16
+    # rate), the burst figure.  A cuBLAS TF32 GEMM measured in this run is
+    # reported beside it as context.  A 3xTF32 GEMM issues three TF32 MMAs
+    # per algorithmic multiply-add.
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    tf32_peak_sustained = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / 2.0
+    tf32_cublas = measure_tf32_peak(torch, dev)
+    # FP32 SIMT peak: 148 SMs x 128 FP32 lanes x 2 FLOP x max SM clock
+    fp32_peak = 148 * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    achieved_tc = 3.0 * g_flops / g_time / 1e12 if g_time > 0 else 0.0
+
     gemm_bench = {}
+    configs = {}
     if rank == 0 and world == 1 and not args.skip_gemm:
         gemm_bench = gemm_sweep(torch, ops, peaks, dev)
-
-    # The TF32 tensor peak is measured here the way the driver measures the
-    # bf16 one: a cuBLAS GEMM (torch.matmul with TF32 enabled), 8192^3, best of
-    # 10, on this GPU -- a library denominator, not part of the timed path.
-    # A 3xTF32 GEMM issues three TF32 MMAs per algorithmic multiply-add.
-    tf32_peak = measure_tf32_peak(torch, dev)
-    achieved_tc = 3.0 * g_flops / g_time / 1e12 if g_time > 0 else 0.0
-    if gemm_bench:
-        # FP32 SIMT peak: 148 SMs x 128 FP32 lanes x 2 FLOP x max SM clock
-        fp32_peak = 148 * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
         r = gemm_bench["8192^3_nn_tflops"]
         gemm_bench["frac_of_peak"] = {
             "3xtf32_tf32_equivalent": round(3.0 * r["3xtf32"] / tf32_peak, 3),
             "tf32": round(r["tf32"] / tf32_peak, 3),
             "fp32_simt": round(r["fp32"] / fp32_peak, 3)}
-        gemm_bench["peaks_tflops"] = {"tf32_cublas_measured": round(tf32_peak, 1),
-                                      "fp32_simt_nominal_at_max_clock": round(fp32_peak, 1)}
+        gemm_bench["peaks_tflops"] = {
+            f"tf32_{peak_kind}_bf16_half": round(tf32_peak, 1),
+            "tf32_cublas_this_run": round(tf32_cublas, 1),
+            "fp32_simt_nominal_at_max_clock": round(fp32_peak, 1)}
         sgemm = measure_cublas_sgemm(torch, dev)
         gemm_bench["cublas_sgemm_8192_tflops"] = round(sgemm, 2)
         gemm_bench["fp32_simt_vs_cublas_sgemm"] = round(r["fp32"] / sgemm, 3)
+    if rank == 0 and world == 1 and not args.skip_configs:
+        configs["square_sweep"] = square_config_sweep(torch, ops, dev, tf32_peak, fp32_peak)
+        configs["ragged"] = ragged_config_sweep(torch, ops, dev, peaks["hbm_gbs"], tf32_peak,
+                                                fp32_peak)
+        configs.update(mlp_config_bench(torch, nn, synthetic, dev, tf32_peak))
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
-        rate, rows, dt, threads = cpu_rate_sample(args.cpu_seconds)
-        cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
-               "sample": f"{rows} rows of the global batch through one full fwd+bwd+SGD step "
-                         f"of the NpArray restatement ({dt:.1f} s)"}
+        cpu = cpu_rate_sample(args.cpu_seconds)
 
     if rank == 0:
         line = {
@@ -437,16 +650,17 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": round(achieved_tc, 1),
                          "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved_tc / tf32_peak, 4),
+                         "frac_of_sustained": round(achieved_tc / tf32_peak_sustained, 4),
+                         "tf32_cublas_this_run": round(tf32_cublas, 1),
                          "traffic": STEP_DX_TRAFFIC_BYTES if B == GLOBAL_BATCH else None,
                          "traffic_note": "DRAM read+write bytes of one dX launch "
                                          "(8192x4096x4096) from an ncu capture of this "
                                          "step; algorithmic 939.5 MB",
                          "kernel": "tc_gemm_kernel<3> (tcgen05 kind::tf32, 3 MMAs per "
                                    "multiply-add), TF32 tensor FLOP = 3 x 2MNK",
-                         "peak_source": "cuBLAS TF32 GEMM 8192^3 measured in this run (best "
-                                        "of 10); for reference "
-                                        f"{peak_kind} bf16_tflops/2 = "
-                                        f"{peaks['bf16_tflops'] / 2.0:.1f}",
+                         "peak_source": f"MEASURED_PEAKS.json bf16_tflops / 2 ({peak_kind}, "
+                                        "burst); frac_of_sustained uses "
+                                        "bf16_tflops_sustained / 2",
                          "gemm_share_of_step": round(g_time / step_gpu_time, 3)
                          if step_gpu_time > 0 else None,
                          "algorithmic_tflops": round(g_flops / g_time / 1e12, 1)
@@ -457,12 +671,15 @@ def run_ours(args):
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk,
             "gemm": gemm_bench,
+            "configs": configs,
+            "dp_check": dp_check,
             "flop_per_sample": FLOP_PER_SAMPLE,
             "model_tflops": round(value * FLOP_PER_SAMPLE / 1e12, 1),
             "final_loss": loss_host[-1] if loss_host else None,
             "step_phases_ms_rank0_eager": phases,
         }
         print(json.dumps(line), flush=True)
+    model.close()  # its NCCL communicator (every rank), before the process group
     if pg is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -516,6 +733,9 @@ def main():
                          "update)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="skip the other BASELINE configs (square sweep, ragged set, MLP "
+                         "3072 and 784)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--gemm", type=int, default=0, metavar="N",
                     help="time only the square N^3 GEMM of --precision (profiling case)")

@@ -12,8 +12,9 @@
  * asynchronous on the context's stream (the legacy default stream unless set),
  * exactly like the reference's cuBLAS call.
  *
- * `handle`: the reference passes an opaque handle (its cuBLAS handle from
- * gpu_init, moonxi-net-gpu/cuda/gpu_context.mbt:67-71).  A handle created by
+ * `handle`: the reference passes an opaque handle (its cuBLAS handle created
+ * by gpu_init, moonxi-net-gpu/cuda/gpu_context.mbt:23-27, and fetched per call
+ * with get_context, :34-39).  A handle created by
  * mx_context_create() selects that context; any other value (NULL, or a
  * cuBLAS handle the caller still passes) selects the default context of the
  * current device.  Unknown handles are never dereferenced.
@@ -35,6 +36,7 @@ extern "C" {
 #define MX_ERR_TIMEOUT 4     /* a bounded in-kernel wait gave up                */
 #define MX_ERR_NOMEM 5       /* workspace allocation failed                     */
 #define MX_ERR_NO_DEVICE 6   /* no usable CUDA device                           */
+#define MX_ERR_COMM 7        /* a collective failed / the communicator is in error */
 
 /* Precision modes for the contraction. */
 #define MX_PREC_DEFAULT 0 /* the context's mode (env MX_MATMUL_PRECISION, else AUTO) */
@@ -146,19 +148,35 @@ int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo, int
  *     anything is launched.
  *   - The first call on a device looks up the device address of that array
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - When the 64 MiB is committed: with CUDA's default lazy module loading,
+ *     when this library's tensor-core module first loads on a device -- the
+ *     first tensor-core GEMM of any entry point, or the first call of this
+ *     one -- and at library load under CUDA_MODULE_LOADING=EAGER.  A caller
+ *     that reserves the rest of the device's memory for its own pool should
+ *     make one call (any size) before reserving it.  If the device has no room
+ *     left at that point the call returns MX_ERR_NOMEM (or MX_ERR_CUDA).
  *   - Every call, on every stream, shares the one array, which keeps the last
  *     call's contents: calls that overlap on the GPU race and corrupt each
  *     other's results.  Serialise them (one stream, or events).
  *   - dev_status: optional device pointer to two int32 words; a bounded
  *     in-kernel wait that gives up writes MX_ERR_TIMEOUT and the call site
- *     there (NULL: into a status word inside the library). */
+ *     there (NULL: into a status word inside the library, read and cleared by
+ *     mx_noalloc_status). */
 int32_t mx_gemm_3xtf32_noalloc(const float* a, const float* b, float* c, const float* bias,
                                int32_t M, int32_t K, int32_t N, int32_t transpose_a,
                                int32_t transpose_b, float alpha, float beta, int32_t relu,
                                int32_t* dev_status, void* stream);
 
+/* Status word of mx_gemm_3xtf32_noalloc calls made with dev_status == NULL on
+ * the current device: synchronises the device, returns the recorded status
+ * (MX_ERR_TIMEOUT if a bounded in-kernel wait gave up, else MX_OK), writes
+ * the call site to `where` (may be NULL) and clears the word.  Allocates
+ * nothing.  No counterpart in the reference. */
+int32_t mx_noalloc_status(int32_t* where);
+
 /* cudaSetDevice for the calling host thread (the reference hard-codes
- * device 0 at every call site, moonxi-net-gpu/cuda/gpu_context.mbt:57-83). */
+ * device 0 at every call site: get_context(0), moonxi-net-gpu/tensor/
+ * trait_impl.mbt:232,265,277,287,311). */
 int32_t moonbit_cuda_set_device(int32_t device);
 
 /* ---------------------------------------------------------------------- */
@@ -166,7 +184,9 @@ int32_t moonbit_cuda_set_device(int32_t device);
 /* ---------------------------------------------------------------------- */
 
 /* Creates a context on `device` (allocates its status word).  NULL on error.
- * Replaces the role of gpu_init's handle (gpu_context.mbt:67-71). */
+ * Replaces the role of gpu_init's handle (gpu_context.mbt:23-27).  Every entry
+ * point that takes a context handle makes the context's device current for
+ * the call and restores the caller's current device before it returns. */
 void* mx_context_create(int32_t device);
 void mx_context_destroy(void* handle);
 int32_t mx_context_set_stream(void* handle, void* stream);
@@ -259,6 +279,72 @@ int32_t mx_sum_squares(void* handle, const float* x, int64_t n, float* out, int3
 int32_t mx_sgd_momentum_clip(void* handle, float* params, const float* grads, float* vels,
                              int64_t n, float lr, float momentum, float weight_decay,
                              float max_grad_norm, const float* norm_sq, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Data-parallel collectives (NCCL over NVLink / NVSwitch)                  */
+/* ---------------------------------------------------------------------- */
+/* The reference has no collectives: its only host loop, run_gpu
+ * (moonxi-net-gpu/train/run.mbt:14-57), trains on one device and reaches
+ * native code only through MOONBIT_FFI_EXPORT stubs
+ * (moonxi-net-gpu/cuda/cuda_stub.c).  These stubs give such a host the
+ * data-parallel step: one process per GPU, a communicator per process, the
+ * weight-gradient all-reduce (or reduce-scatter + all-gather for a sharded
+ * update) on a stream of the caller's choice.  NCCL is loaded at run time;
+ * without it every call returns MX_ERR_UNSUPPORTED.  Handles are never
+ * dereferenced when unknown (MX_ERR_INVALID). */
+#define MX_NCCL_UNIQUE_ID_BYTES 128
+
+/* NCCL version (e.g. 22809), or -1 when NCCL cannot be loaded. */
+int32_t moonbit_nccl_version(void);
+/* Fills id[128] with a fresh NCCL unique id: rank 0 makes it and hands the
+ * bytes to every other rank by any side channel. */
+int32_t moonbit_nccl_get_unique_id(uint8_t* id);
+/* Communicator of `rank` in `world` ranks on `device` from the shared id
+ * (every rank calls it; it returns once all have).  NULL on failure, with
+ * the reason in moonbit_nccl_last_status().  Like the reference's
+ * moonbit_cublas_create (cuda_stub.c:240-242), the handle is a plain void*. */
+void* moonbit_nccl_init(const uint8_t* id, int32_t rank, int32_t world, int32_t device);
+/* moonbit_nccl_init with a file as the side channel, for hosts that have no
+ * other: rank 0 writes a fresh id to `path` (written to a temporary name and
+ * renamed, so readers never see part of it), the other ranks wait up to
+ * timeout_ms for it (then NULL with MX_ERR_TIMEOUT).  Delete the file after
+ * every rank has initialised. */
+void* moonbit_nccl_init_file(const char* path, int32_t rank, int32_t world, int32_t device,
+                             int32_t timeout_ms);
+/* Status of the calling thread's last moonbit_nccl_init / _init_file. */
+int32_t moonbit_nccl_last_status(void);
+int32_t moonbit_nccl_comm_info(void* comm, int32_t* rank, int32_t* world, int32_t* device);
+/* Sum of `count` floats over all ranks, enqueued on `stream` (NULL = legacy
+ * default stream); send == recv is the in-place form. */
+int32_t moonbit_nccl_allreduce_sum_f32(void* comm, const float* send, float* recv, int64_t count,
+                                       void* stream);
+/* recv[recv_count] = this rank's piece of the sum of send[world *
+ * recv_count]; in place when recv == send + rank * recv_count. */
+int32_t moonbit_nccl_reduce_scatter_sum_f32(void* comm, const float* send, float* recv,
+                                            int64_t recv_count, void* stream);
+/* recv[world * send_count] = every rank's send[send_count] in rank order; in
+ * place when send == recv + rank * send_count. */
+int32_t moonbit_nccl_all_gather_f32(void* comm, const float* send, float* recv,
+                                    int64_t send_count, void* stream);
+/* recv[count] = root's send[count] (send is read on the root only). */
+int32_t moonbit_nccl_broadcast_f32(void* comm, const float* send, float* recv, int64_t count,
+                                   int32_t root, void* stream);
+/* Brackets several collectives into one launch (ncclGroupStart/End). */
+int32_t moonbit_nccl_group_start(void);
+int32_t moonbit_nccl_group_end(void);
+/* MX_OK while the communicator is healthy, MX_ERR_COMM once NCCL has
+ * recorded an asynchronous error (e.g. a peer that went away). */
+int32_t moonbit_nccl_get_async_error(void* comm);
+/* Host-side watchdog: waits until `stream` has drained, polling the
+ * communicator's asynchronous error.  On an error (MX_ERR_COMM) or after
+ * timeout_ms (MX_ERR_TIMEOUT) it aborts the communicator -- its kernels stop
+ * waiting for peers -- and the handle becomes invalid.  The reference aborts
+ * the whole process on any failure instead (gpu_tensor.mbt:12-16). */
+int32_t moonbit_nccl_wait(void* comm, void* stream, int32_t timeout_ms);
+/* Aborts the communicator (ncclCommAbort); the handle becomes invalid. */
+int32_t moonbit_nccl_abort(void* comm);
+/* Finalises and destroys the communicator; every rank calls it. */
+int32_t moonbit_nccl_destroy(void* comm);
 
 #ifdef __cplusplus
 }

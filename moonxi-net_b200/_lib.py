@@ -22,6 +22,8 @@ MX_ERR_CUDA = 3
 MX_ERR_TIMEOUT = 4
 MX_ERR_NOMEM = 5
 MX_ERR_NO_DEVICE = 6
+MX_ERR_COMM = 7
+NCCL_UNIQUE_ID_BYTES = 128
 
 PREC_DEFAULT = 0
 PREC_AUTO = 1
@@ -61,6 +63,7 @@ SIGNATURES = {
                                               _vp, _vp, _vp, _vp]),
     "mx_gemm_3xtf32_noalloc":(_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,
                                       _f32, _i32, _vp, _vp]),
+    "mx_noalloc_status": (_i32, [ctypes.POINTER(_i32)]),
     "moonbit_cuda_set_device": (_i32, [_i32]),
     "mx_context_create": (_vp, [_i32]),
     "mx_context_destroy": (None, [_vp]),
@@ -80,6 +83,23 @@ SIGNATURES = {
                                         _vp]),
     "mx_sum_squares": (_i32, [_vp, _vp, _i64, _vp, _i32, _vp]),
     "mx_sgd_momentum_clip": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _vp, _vp]),
+    "moonbit_nccl_version": (_i32, []),
+    "moonbit_nccl_get_unique_id": (_i32, [_vp]),
+    "moonbit_nccl_init": (_vp, [_vp, _i32, _i32, _i32]),
+    "moonbit_nccl_init_file": (_vp, [ctypes.c_char_p, _i32, _i32, _i32, _i32]),
+    "moonbit_nccl_last_status": (_i32, []),
+    "moonbit_nccl_comm_info": (_i32, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                                      ctypes.POINTER(_i32)]),
+    "moonbit_nccl_allreduce_sum_f32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
+    "moonbit_nccl_reduce_scatter_sum_f32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
+    "moonbit_nccl_all_gather_f32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
+    "moonbit_nccl_broadcast_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp]),
+    "moonbit_nccl_group_start": (_i32, []),
+    "moonbit_nccl_group_end": (_i32, []),
+    "moonbit_nccl_get_async_error": (_i32, [_vp]),
+    "moonbit_nccl_wait": (_i32, [_vp, _vp, _i32]),
+    "moonbit_nccl_abort": (_i32, [_vp]),
+    "moonbit_nccl_destroy": (_i32, [_vp]),
 }
 
 
@@ -104,6 +124,11 @@ def build() -> str:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
+        # torch first: the library's collective stubs load NCCL by its soname
+        # (libnccl.so.2) on first use, and whichever NCCL is loaded first is
+        # the one every later user binds to.  torch needs its own (newer)
+        # build, so it must win; the stubs then share it.
+        import torch  # noqa: F401
         if not os.path.exists(LIB_PATH):
             raise ImportError(
                 f"moonxi_net_b200: native library missing at {LIB_PATH}; run "

@@ -73,13 +73,19 @@ int init_context(Context* c, int device) {
 
 // The context for `handle`: a registered context, else the current device's
 // default context (created on first use).  Never dereferences unknown handles.
-Context* resolve(void* handle) {
+// A registered context on another device is made current; *prev receives the
+// device to restore afterwards (-1 when nothing was switched).
+Context* resolve(void* handle, int* prev) {
+  *prev = -1;
   std::lock_guard<std::mutex> lk(g_mu);
   Context* c = static_cast<Context*>(handle);
   if (c && g_contexts.count(c)) {
     int cur = -1;
     cudaGetDevice(&cur);
-    if (cur != c->device) cudaSetDevice(c->device);
+    if (cur != c->device) {
+      if (cudaSetDevice(c->device) != cudaSuccess) return nullptr;
+      *prev = cur;
+    }
     return c;
   }
   int dev = 0;
@@ -94,6 +100,21 @@ Context* resolve(void* handle) {
   }
   return g_default[dev];
 }
+
+// An entry point's context for the duration of the call: the context's
+// device is current inside the call, and the caller's current device is
+// restored on return (a host thread that drives several devices keeps its
+// own device selection).
+struct Scoped {
+  Context* c = nullptr;
+  int prev = -1;
+  explicit Scoped(void* handle) { c = resolve(handle, &prev); }
+  ~Scoped() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  Scoped(const Scoped&) = delete;
+  Scoped& operator=(const Scoped&) = delete;
+};
 
 cudaStream_t pick_stream(Context* c, void* stream) {
   return stream ? static_cast<cudaStream_t>(stream) : c->stream;
@@ -263,7 +284,8 @@ using namespace mx;
 // ------------------------------------------------------------------ matmul
 MX_EXPORT int cuda_matmul(void* handle, float* a, float* b, float* c, int M, int K, int N,
                           int transpose_a, int transpose_b, float alpha, float beta) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   return run_gemm(ctx, ref_args(a, b, c, M, K, N, transpose_a, transpose_b, alpha, beta),
                   MX_PREC_DEFAULT, ctx->stream);
@@ -280,7 +302,8 @@ MX_EXPORT int32_t moonbit_cuda_matmul_ex(void* handle, void* a, void* b, void* c
                                          int32_t K, int32_t N, int32_t transpose_a,
                                          int32_t transpose_b, float alpha, float beta,
                                          void* stream, int32_t precision) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   return run_gemm(ctx,
                   ref_args(static_cast<float*>(a), static_cast<float*>(b), static_cast<float*>(c),
@@ -292,7 +315,8 @@ MX_EXPORT int32_t moonbit_cuda_linear_fwd_ex(void* handle, void* x, void* w, voi
                                              int32_t M, int32_t K, int32_t N,
                                              int32_t transpose_w, int32_t relu, float alpha,
                                              void* stream, int32_t precision) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   GemmArgs g = ref_args(static_cast<float*>(x), static_cast<float*>(w), static_cast<float*>(y), M,
                         K, N, 0, transpose_w, alpha, 0.0f);
@@ -313,7 +337,8 @@ MX_EXPORT int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float
                              int32_t transpose_a, int32_t transpose_b, int64_t lda, int64_t ldb,
                              int64_t ldc, float alpha, float beta, int32_t relu, void* stream,
                              int32_t precision) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   GemmArgs g = ref_args(const_cast<float*>(a), const_cast<float*>(b), c, M, K, N, transpose_a,
                         transpose_b, alpha, beta);
@@ -330,7 +355,8 @@ MX_EXPORT int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float
 
 MX_EXPORT int32_t mx_split_tf32(void* handle, const float* src, int32_t rows, int32_t cols,
                                 int64_t ld, float* hi, float* lo, int64_t ld_out, void* stream) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   if (rows < 0 || cols < 0 || ld < cols || ld_out < cols) return MX_ERR_INVALID;
   if (rows > 0 && cols > 0 && (!src || !hi)) return MX_ERR_INVALID;
@@ -345,7 +371,8 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
                                    int32_t N, float alpha, float beta, const float* bias,
                                    int32_t relu, const float* mask, int64_t ldm, int32_t passes,
                                    int32_t flags, void* stream) {
-  Context* ctx = resolve(handle);
+  Scoped scope(handle);
+  Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   if (M < 0 || N < 0 || K < 1) return MX_ERR_INVALID;
   if (lda < (a_kmajor ? K : M) || ldb < (b_kmajor ? K : N) || ldc < N) return MX_ERR_INVALID;
@@ -402,14 +429,16 @@ MX_EXPORT void mx_context_destroy(void* handle) {
 }
 
 MX_EXPORT int32_t mx_context_set_stream(void* handle, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   c->stream = static_cast<cudaStream_t>(stream);
   return MX_OK;
 }
 
 MX_EXPORT int32_t mx_context_set_precision(void* handle, int32_t precision) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (precision < MX_PREC_DEFAULT || precision > MX_PREC_NPARRAY) return MX_ERR_INVALID;
   c->precision = precision == MX_PREC_DEFAULT ? env_precision() : precision;
@@ -417,7 +446,8 @@ MX_EXPORT int32_t mx_context_set_precision(void* handle, int32_t precision) {
 }
 
 MX_EXPORT int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (ns == 0) return MX_ERR_INVALID;
   c->timeout_ns = ns;
@@ -425,7 +455,8 @@ MX_EXPORT int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns) {
 }
 
 MX_EXPORT int32_t mx_context_reserve_workspace(void* handle, uint64_t bytes) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   int rc = ensure_workspace(c, bytes);
   if (rc == kOk) rc = ensure_small_scratch(c, 1 << 20);
@@ -435,7 +466,8 @@ MX_EXPORT int32_t mx_context_reserve_workspace(void* handle, uint64_t bytes) {
 MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K, int32_t N,
                                              int32_t transpose_a, int32_t transpose_b,
                                              int32_t precision) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c || M <= 0 || N <= 0 || K < 0) return 0;
   GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
   const int p = resolve_precision(c, M, K, N, precision);
@@ -447,7 +479,8 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
 }
 
 MX_EXPORT int32_t mx_context_status(void* handle, int32_t* where) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e);
@@ -461,7 +494,8 @@ MX_EXPORT int32_t mx_context_status(void* handle, int32_t* where) {
 
 MX_EXPORT int32_t mx_matmul_resolve_precision(void* handle, int32_t M, int32_t K, int32_t N,
                                               int32_t precision) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   return resolve_precision(c, M, K, N, precision);
 }
@@ -475,6 +509,7 @@ MX_EXPORT const char* mx_status_string(int32_t status) {
     case MX_ERR_TIMEOUT: return "bounded in-kernel wait timed out";
     case MX_ERR_NOMEM: return "workspace allocation failed";
     case MX_ERR_NO_DEVICE: return "no usable CUDA device";
+    case MX_ERR_COMM: return "collective communication failed";
     default: return "unknown status";
   }
 }
@@ -484,7 +519,8 @@ MX_EXPORT uint64_t mx_kernel_launch_count(void) { return g_launches.load(); }
 // ------------------------------------------------------- training-step ops
 MX_EXPORT int32_t mx_relu_backward(void* handle, const float* grad_out, const float* saved,
                                    float* grad_in, int64_t n, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (n < 0 || (n > 0 && (!grad_out || !saved || !grad_in))) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
@@ -493,7 +529,8 @@ MX_EXPORT int32_t mx_relu_backward(void* handle, const float* grad_out, const fl
 
 MX_EXPORT int32_t mx_reduce_sum_leading(void* handle, const float* in, float* out,
                                         int32_t output_numel, int32_t lead_stride, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (output_numel < 0 || lead_stride < 0 || (output_numel > 0 && (!in || !out)))
     return MX_ERR_INVALID;
@@ -504,7 +541,8 @@ MX_EXPORT int32_t mx_reduce_sum_leading(void* handle, const float* in, float* ou
 MX_EXPORT int32_t mx_softmax_ce_labels(void* handle, const float* logits, const float* labels,
                                        float* grad, float* loss, int32_t batch,
                                        int32_t num_classes, int32_t denom, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (!logits || !labels || batch <= 0 || num_classes <= 0 || denom <= 0) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
@@ -516,7 +554,8 @@ MX_EXPORT int32_t mx_softmax_ce_labels_split(void* handle, const float* logits,
                                              const float* labels, float* grad, float* g_hi,
                                              float* g_lo, float* loss, int32_t batch,
                                              int32_t num_classes, int32_t denom, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (!logits || !labels || !grad || !g_hi || !g_lo || batch <= 0 || num_classes <= 0 ||
       denom <= 0)
@@ -533,7 +572,8 @@ MX_EXPORT int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, co
                                                  float momentum, float weight_decay,
                                                  float max_grad_norm, float* norm_out,
                                                  float* p_hi, float* p_lo, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (n < 0 || (n > 0 && (!params || !grads || !vels || !p_hi || !p_lo))) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
@@ -545,7 +585,8 @@ MX_EXPORT int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, co
 
 MX_EXPORT int32_t mx_sum_squares(void* handle, const float* x, int64_t n, float* out,
                                  int32_t accumulate, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (n < 0 || !out || (n > 0 && !x)) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
@@ -556,7 +597,8 @@ MX_EXPORT int32_t mx_sgd_momentum_clip(void* handle, float* params, const float*
                                        float* vels, int64_t n, float lr, float momentum,
                                        float weight_decay, float max_grad_norm,
                                        const float* norm_sq, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (n < 0 || !norm_sq || (n > 0 && (!params || !grads || !vels))) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);
@@ -570,7 +612,8 @@ MX_EXPORT int32_t mx_sgd_momentum_autoclip(void* handle, float* params, const fl
                                            float* vels, int64_t n, float lr, float momentum,
                                            float weight_decay, float max_grad_norm,
                                            float* norm_out, void* stream) {
-  Context* c = resolve(handle);
+  Scoped scope(handle);
+  Context* c = scope.c;
   if (!c) return MX_ERR_NO_DEVICE;
   if (n < 0 || (n > 0 && (!params || !grads || !vels))) return MX_ERR_INVALID;
   cudaStream_t s = pick_stream(c, stream);

@@ -386,10 +386,7 @@ __global__ void __launch_bounds__(kThreads, Shape<BN>::kCtasPerSm)
       const int issued_end = min(nkb, max(it - 1, 0) + kStages);
       for (int j = it; j < issued_end; ++j) {
         const int s = j % kStages;
-        uint64_t t0 = globaltimer_ns();
-        while (!bar_try_wait(&full[s], (j / kStages) & 1) &&
-               globaltimer_ns() - t0 < p.timeout_ns) {
-        }
+        drain_wait(&full[s], (j / kStages) & 1, p.status, 102);
       }
     }
   } else {
@@ -528,9 +525,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     if (!ok && tid == 0) {
       // let every load this CTA issued land before the CTA exits (bounded)
       for (int j = landed; j < issued; ++j) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!bar_try_wait(&full[j % S], (j / S) & 1) && globaltimer_ns() - t0 < p.timeout_ns) {
-        }
+        drain_wait(&full[j % S], (j / S) & 1, p.status, 115);
       }
     }
     return;
@@ -584,15 +579,9 @@ cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const S
                            dim3 grid, cudaStream_t s) {
   auto kern = simt_gemm_kernel<BN, AK, BKC, TMA, STRICT>;
   constexpr int kSmemBytes = Shape<BN>::kSmemBytes;
-  static unsigned configured = 0;  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured |= 1u << (dev & 31);
-  }
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(kern, kSmemBytes);
+  if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, kSmemBytes, s>>>(ta, tb, p);
   note_launches(1);
   return cudaGetLastError();
@@ -629,15 +618,9 @@ template <bool AK, bool BKC>
 cudaError_t launch_ws_variant(const CUtensorMap& ta, const CUtensorMap& tb, const SimtParams& p,
                               dim3 grid, cudaStream_t s) {
   auto kern = simt_ws_kernel<AK, BKC>;
-  static unsigned configured = 0;  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured |= 1u << (dev & 31);
-  }
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(kern, kWsSmemBytes);
+  if (e != cudaSuccess) return e;
   kern<<<grid, kWsThreads, kWsSmemBytes, s>>>(ta, tb, p);
   note_launches(1);
   return cudaGetLastError();

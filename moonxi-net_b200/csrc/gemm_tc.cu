@@ -456,13 +456,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // Every copy this thread issued must land before the CTA can exit.
-      for (int s = 0; s < C::kStages; ++s) {
-        if (!armed[s]) continue;
-        const uint64_t t0 = globaltimer_ns();
-        while (!bar_try_wait(&full[s], armed_parity[s]) && globaltimer_ns() - t0 < p.timeout_ns) {
-        }
-      }
+      // Every copy this thread issued must land before the CTA can exit
+      // (bounded by the drain limit, not by the caller's wait limit).
+      for (int s = 0; s < C::kStages; ++s)
+        if (armed[s]) drain_wait(&full[s], armed_parity[s], p.status, 207);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -523,9 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Wait for every MMA this thread issued before TMEM is released.
       tc_commit(drain);
-      const uint64_t t0 = globaltimer_ns();
-      while (!bar_try_wait(drain, 0) && globaltimer_ns() - t0 < p.timeout_ns) {
-      }
+      drain_wait(drain, 0, p.status, 208);
     }
     __syncwarp();
   } else {
@@ -753,14 +748,9 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
                       const CUtensorMap& bl, const TcParams& p, int grid, cudaStream_t s) {
   auto kern = tc_gemm_kernel<PASSES, AK, BKM>;
   constexpr int kSmem = Cfg<PASSES, stage_bk<PASSES, AK, BKM>()>::kSmem;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess) return e;
-    configured |= 1u << (dev & 31);
-  }
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(kern, kSmem);
+  if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, kSmem, s>>>(ah, al, bh, bl, p);
   note_launches(1);
   return cudaGetLastError();
@@ -1090,4 +1080,26 @@ extern "C" __attribute__((visibility("default"))) int32_t mx_gemm_3xtf32_noalloc
   p.timeout_ns = 2000000000ull;
   e = launch_tc<3, true, true>(tah, tal, tbh, tbl, p, std::min(p.num_tiles, d->num_sms), s);
   return e == cudaSuccess ? kOk : cuda_status(e);
+}
+
+// Reads and clears the library's own status word of the allocation-free
+// entry point on the current device (the word its kernels write when the
+// caller passes no dev_status).  Synchronises the device first.  No
+// allocation: the word is part of the same static data as the scratch.
+extern "C" __attribute__((visibility("default"))) int32_t mx_noalloc_status(int32_t* where) {
+  using namespace mx;
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_setup(&d);
+  if (rc != kOk) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e);
+  int st[2] = {0, 0};
+  e = cudaMemcpy(st, d->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (where) *where = st[1];
+  if (st[0] != 0) {
+    e = cudaMemset(d->status, 0, sizeof(st));
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return st[0];
 }

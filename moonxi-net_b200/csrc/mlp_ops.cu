@@ -122,20 +122,34 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Class index of a label stored as a float.  A label outside [0, C) (or NaN)
+// would index past the logits row: it records MX_ERR_INVALID with call site
+// `where` in the status word and returns -1 (the row then gets no one-hot
+// term and a NaN loss).  The reference reads such a row out of bounds.
+__device__ __forceinline__ int checked_label(float lf, int C, int* status, int where) {
+  if (lf >= 0.0f && lf < static_cast<float>(C)) return static_cast<int>(lf);
+  if (status) {
+    atomicCAS(status, kOk, kErrInvalid);
+    atomicCAS(status + 1, 0, where);
+  }
+  return -1;
+}
+
 // One warp per row; 8 rows per block.  exp/log are evaluated in double and
 // rounded to float, as NpArray does (image_impl.mbt:95-103).  Writes the
 // block's partial loss (sum of its rows' -log p[label]) to partial[block].
 __global__ void softmax_ce_kernel(const float* __restrict__ logits,
                                   const float* __restrict__ labels, float* __restrict__ grad,
                                   float* __restrict__ g_hi, float* __restrict__ g_lo,
-                                  float* __restrict__ partial, int batch, int C, float denom) {
+                                  float* __restrict__ partial, int batch, int C, float denom,
+                                  int* __restrict__ status) {
   __shared__ float row_loss[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x * 8 + warp;
   float loss = 0.0f;
   if (b < batch) {
     const float* row = logits + static_cast<int64_t>(b) * C;
-    const int label = static_cast<int>(labels[b]);
+    const int label = checked_label(labels[b], C, status, 301);
     float mx_ = -INFINITY;
     for (int j = lane; j < C; j += 32) mx_ = fmaxf(mx_, row[j]);
     mx_ = warp_max(mx_);
@@ -145,8 +159,9 @@ __global__ void softmax_ce_kernel(const float* __restrict__ logits,
     se = warp_sum(se);
     const float lse = static_cast<float>(log(static_cast<double>(se)));
     if (lane == 0) {
-      const float lp = __fsub_rn(__fsub_rn(row[label], mx_), lse);
-      loss = -lp;
+      // an out-of-range label has no log-probability: the row's loss is NaN
+      // (and the status word says why)
+      loss = label >= 0 ? -__fsub_rn(__fsub_rn(row[label], mx_), lse) : __int_as_float(0x7fc00000);
     }
     if (grad) {
       float* g = grad + static_cast<int64_t>(b) * C;
@@ -317,11 +332,12 @@ __global__ void reduce_leading_seq_kernel(const float* __restrict__ in, float* _
 // ascending; row_loss[b] = -log p[label].
 __global__ void softmax_ce_seq_kernel(const float* __restrict__ logits,
                                       const float* __restrict__ labels, float* __restrict__ grad,
-                                      float* __restrict__ row_loss, int batch, int C, float denom) {
+                                      float* __restrict__ row_loss, int batch, int C, float denom,
+                                      int* __restrict__ status) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   const float* row = logits + static_cast<int64_t>(b) * C;
-  const int label = static_cast<int>(labels[b]);
+  const int label = checked_label(labels[b], C, status, 302);
   float mx_ = row[0];
   for (int j = 1; j < C; ++j)
     if (row[j] > mx_) mx_ = row[j];
@@ -329,7 +345,8 @@ __global__ void softmax_ce_seq_kernel(const float* __restrict__ logits,
   for (int j = 0; j < C; ++j)
     se = __fadd_rn(se, static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))));
   const float lse = static_cast<float>(log(static_cast<double>(se)));
-  row_loss[b] = -__fsub_rn(__fsub_rn(row[label], mx_), lse);
+  row_loss[b] = label >= 0 ? -__fsub_rn(__fsub_rn(row[label], mx_), lse)
+                           : __int_as_float(0x7fc00000);
   if (grad) {
     float* g = grad + static_cast<int64_t>(b) * C;
     for (int j = 0; j < C; ++j) {
@@ -408,8 +425,8 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
     int rc = ensure_small_scratch(ctx, static_cast<size_t>(batch) * sizeof(float));
     if (rc != kOk) return rc;
     float* row_loss = static_cast<float*>(ctx->small_scratch);
-    softmax_ce_seq_kernel<<<(batch + 127) / 128, 128, 0, s>>>(logits, labels, grad, row_loss,
-                                                              batch, C, static_cast<float>(denom));
+    softmax_ce_seq_kernel<<<(batch + 127) / 128, 128, 0, s>>>(
+        logits, labels, grad, row_loss, batch, C, static_cast<float>(denom), ctx->status);
     note_launches(1);
     if (loss) {
       seq_sum_kernel<<<1, 1, 0, s>>>(row_loss, batch, static_cast<float>(denom), loss, 0);
@@ -422,7 +439,7 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
   if (rc != kOk) return rc;
   float* partial = static_cast<float*>(ctx->small_scratch);
   softmax_ce_kernel<<<blocks, 256, 0, s>>>(logits, labels, grad, g_hi, g_lo, partial, batch, C,
-                                           static_cast<float>(denom));
+                                           static_cast<float>(denom), ctx->status);
   note_launches(1);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e);

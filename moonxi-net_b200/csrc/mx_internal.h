@@ -4,13 +4,15 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 
 namespace mx {
 
 // Per-device execution context.  The reference passes an opaque handle to
-// every matmul (a cuBLAS handle, moonxi-net-gpu/cuda/gpu_context.mbt:67-71);
+// every matmul (a cuBLAS handle created by gpu_init,
+// moonxi-net-gpu/cuda/gpu_context.mbt:23-27);
 // this library's handle is a Context, or NULL for the per-device default.
 struct Context {
   int device = 0;
@@ -150,5 +152,26 @@ int cuda_status(cudaError_t e);
 
 // Counts kernel launches (diagnostic, exported as mx_kernel_launch_count).
 void note_launches(int n);
+
+// Raises a kernel's dynamic shared-memory limit once per device.  One static
+// instance per kernel; safe from several host threads (a race only repeats
+// the idempotent attribute call).  Devices beyond the table are configured on
+// every launch.
+struct SmemOptIn {
+  static constexpr int kMaxDevices = 64;
+  std::atomic<bool> done[kMaxDevices] = {};
+  template <typename Kernel>
+  cudaError_t ensure(Kernel kern, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire))
+      return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices)
+      done[dev].store(true, std::memory_order_release);
+    return e;
+  }
+};
 
 }  // namespace mx

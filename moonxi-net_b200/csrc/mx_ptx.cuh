@@ -84,6 +84,31 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Bound on the waits of the abort path (in-flight TMA copies landing, issued
+// MMAs completing before TMEM is freed).  It is separate from the caller's
+// wait limit: a caller may shorten that limit to microseconds, but work that
+// was already issued always gets this long to finish before the CTA exits.
+constexpr uint64_t kDrainNs = 1000000000ull;
+
+// Bounded wait of the abort path for a phase that work already in flight
+// will complete.  Returns false (and records kErrTimeout with `where` unless
+// a status is already recorded) if it did not complete within kDrainNs.
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, int* status,
+                                           int where) {
+  if (bar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!bar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kDrainNs) {
+      if (status) {
+        atomicCAS(status, kOk, kErrTimeout);
+        atomicCAS(status + 1, 0, where);
+      }
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

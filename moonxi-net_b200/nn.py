@@ -23,7 +23,10 @@ over the ranks of a ``torch.distributed`` process group; the loss is scaled by
 1/global_batch so the sum over ranks equals the single-device mean; each
 layer's (dW, db) bucket is all-reduced (NCCL over NVLink) as soon as its
 GEMMs are queued, so the reduction of layer i overlaps the backward GEMMs of
-layers i-1..1; every replica then applies the identical update.
+layers i-1..1; every replica then applies the identical update.  On an NCCL
+group the collectives go through the library's own ``moonbit_nccl_*`` stubs
+(collectives.NcclCollectives; torch.distributed only bootstraps the
+communicator), on a gloo group through torch.distributed.
 """
 from __future__ import annotations
 
@@ -31,6 +34,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .collectives import as_collectives
 
 _ALIGN = 64  # floats: every parameter block starts on a 256-byte boundary
 _LOSS_SLOTS = _ALIGN  # the per-step loss rides in front of the first bucket
@@ -121,18 +125,17 @@ class ShardPlan:
         return out
 
     def reduce_scatter(self, buf, i, group, async_op=True):
-        """Sums bucket i of `buf` over the ranks into this rank's piece."""
-        import torch.distributed as dist
+        """Sums bucket i of `buf` over the ranks into this rank's piece.
+        `group`: a process group (None = default) or a collectives object."""
         s, e = self.buckets[i]
         a, b = self.pieces[i]
-        return dist.reduce_scatter_tensor(buf[a:b], buf[s:e], group=group, async_op=async_op)
+        return as_collectives(group).reduce_scatter(buf[a:b], buf[s:e], async_op=async_op)
 
     def all_gather(self, buf, i, group, async_op=True):
         """Fills bucket i of `buf` with every rank's piece."""
-        import torch.distributed as dist
         s, e = self.buckets[i]
         a, b = self.pieces[i]
-        return dist.all_gather_into_tensor(buf[s:e], buf[a:b], group=group, async_op=async_op)
+        return as_collectives(group).all_gather(buf[s:e], buf[a:b], async_op=async_op)
 
 
 def shard_rows(global_batch: int, rank: int, world: int):
@@ -153,7 +156,7 @@ class MLP:
     def __init__(self, dims, weights=None, biases=None, layout: str = "nn", device=None,
                  precision="default", lr: float = 0.01, momentum: float = 0.9,
                  weight_decay: float = 1e-4, max_grad_norm: float = 35.0,
-                 process_group=None, fused=None, shard_update=None):
+                 process_group=None, fused=None, shard_update=None, collectives=None):
         if layout not in ("nn", "nt"):
             raise ValueError("layout must be 'nn' (w [in,out]) or 'nt' (w [out,in])")
         self.dims = list(dims)
@@ -169,12 +172,24 @@ class MLP:
         self.weight_decay, self.max_grad_norm = float(weight_decay), float(max_grad_norm)
         self.pg = process_group
         self.rank = 0
+        # collectives: None = the group's default (the library's NCCL stubs on
+        # an NCCL group, torch.distributed otherwise), "torch" = always
+        # torch.distributed, or a collectives object to share
+        self.coll = None
         if process_group is not None:
             import torch.distributed as dist
             self.world = dist.get_world_size(process_group)
             self.rank = dist.get_rank(process_group)
+            if collectives == "torch":
+                from .collectives import TorchCollectives
+                self.coll = TorchCollectives(process_group)
+            elif collectives is not None:
+                self.coll = collectives
+            else:
+                self.coll = as_collectives(process_group, self.device)
         else:
             self.world = 1
+        self._owns_coll = collectives is None and self.coll is not None
         # Split-form path (3xTF32 with every operand kept as hi/lo copies written
         # by its producer): needs TMA-legal leading dimensions (multiples of 4).
         self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
@@ -283,7 +298,7 @@ class MLP:
         if not self.sharded:
             return
         bufs = [self._params_full] + ([self._vels_full] if vels else [])
-        works = [self.plan.all_gather(buf, i, self.pg) for buf in bufs for i in range(self.L)]
+        works = [self.plan.all_gather(buf, i, self.coll) for buf in bufs for i in range(self.L)]
         for wk in works:
             wk.wait()
         ops.split_tf32(self.params, self.params_hi, self.params_lo, ctx=self.ctx)
@@ -370,9 +385,8 @@ class MLP:
             else:    # dW[in,out] = X^T dY
                 timed(2 * B * fi * fo, ops.matmul, h[i], g, fi, B, fo, ta=True, tb=False,
                       out=self.gw[i], ctx=ctx)
-            if self.pg is not None:
-                import torch.distributed as dist
-                works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
+            if self.coll is not None:
+                works.append(self.coll.all_reduce(self.bucket(i)))
             if i > 0:
                 gprev = gbuf[i - 1]
                 # dX = dY W^T: w [in,out] -> stored [N=in, K=out] (tb=1); w [out,in] -> tb=0
@@ -425,7 +439,7 @@ class MLP:
         if plan is not None:
             # the new weights: every rank's pieces, layer by layer, on the
             # collective stream while the forward of the earlier layers runs
-            gathers = [plan.all_gather(self._params_full, i, self.pg) for i in range(self.L)]
+            gathers = [plan.all_gather(self._params_full, i, self.coll) for i in range(self.L)]
         xh, xl = hsplit[0]
         ops.split_tf32(x, xh, xl, ctx=ctx)
         # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
@@ -457,7 +471,7 @@ class MLP:
             # is all-reduced chunk by chunk as the chunks are computed
             Mrows, Ncols = (fo, fi) if nt else (fi, fo)
             nchunk = (self.last_bucket_chunks
-                      if (self.pg is not None and plan is None and i == 0) else 1)
+                      if (self.coll is not None and plan is None and i == 0) else 1)
             rows_per = -(-Mrows // nchunk)
             rows_per = -(-rows_per // 128) * 128
             bstart, bend = self.layout_.bucket(i)
@@ -472,18 +486,15 @@ class MLP:
                     gemm(2 * B * (r1 - r0) * Ncols, a_hi=hh.view(-1)[r0:], a_lo=hl.view(-1)[r0:],
                          lda=fi, a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo, b_kmajor=False,
                          M=r1 - r0, K=B, N=fo, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
-                if self.pg is not None and nchunk > 1:
-                    import torch.distributed as dist
+                if self.coll is not None and nchunk > 1:
                     lo = bstart if r0 == 0 else _LOSS_SLOTS + self.w_off[i] + r0 * Ncols
                     hi = bend if r1 == Mrows else _LOSS_SLOTS + self.w_off[i] + r1 * Ncols
-                    works.append(dist.all_reduce(self.grads_buf[lo:hi], group=self.pg,
-                                                 async_op=True))
+                    works.append(self.coll.all_reduce(self.grads_buf[lo:hi]))
                 r0 = r1
             if plan is not None:
-                works.append(plan.reduce_scatter(self.grads_buf, i, self.pg))
-            elif self.pg is not None and nchunk == 1:
-                import torch.distributed as dist
-                works.append(dist.all_reduce(self.bucket(i), group=self.pg, async_op=True))
+                works.append(plan.reduce_scatter(self.grads_buf, i, self.coll))
+            elif self.coll is not None and nchunk == 1:
+                works.append(self.coll.all_reduce(self.bucket(i)))
             if i > 0:
                 # dX = (dY W^T) masked by relu'(h_i); split copy for the next GEMMs
                 ph, pl = gsplit[i - 1]
@@ -510,7 +521,6 @@ class MLP:
         all-reduce that also sums the loss), then the update of this rank's
         pieces.  The new split copies are made after the next step's
         all-gather, so the update writes p and v only."""
-        import torch.distributed as dist
         ranges = self.plan.update_ranges()
         sc = self.scalars
         if ranges:
@@ -518,7 +528,7 @@ class MLP:
                 ops.sum_squares(self.grads_buf[a:b], sc[0:1], accumulate=k > 0, ctx=self.ctx)
         else:
             ops.sum_squares(self.grads_buf[:0], sc[0:1], ctx=self.ctx)
-        dist.all_reduce(sc, group=self.pg)
+        self.coll.all_reduce(sc).wait()
         if update:
             for a, b in ranges:
                 ops.sgd_momentum_clip(self._params_full[a:b], self.grads_buf[a:b],
@@ -544,6 +554,15 @@ class MLP:
 
     def release_graph(self):
         self._graph = None
+
+    def close(self):
+        """Releases the captured step and, when this model made its own NCCL
+        communicator, destroys it (every rank calls close; graphs holding
+        its collectives go first)."""
+        self._graph = None
+        if self.coll is not None and self._owns_coll:
+            self.coll.destroy()
+        self.coll = None
 
 
 class HostBatchPipeline:

@@ -254,8 +254,14 @@ def sgd_momentum_clip(params, grads, vels, lr, momentum, weight_decay, max_grad_
 
 def status(device: int | None = None) -> tuple[int, int]:
     """(status, call site) of the device status word; synchronises, clears it."""
+    return context_status(context(device))
+
+
+def context_status(ctx) -> tuple[int, int]:
+    """(status, call site) of one context's status word (mx_context_status):
+    synchronises the context's device, clears the word."""
     where = ctypes.c_int32(0)
-    rc = _lib.lib().mx_context_status(context(device), ctypes.byref(where))
+    rc = _lib.lib().mx_context_status(ctx, ctypes.byref(where))
     return rc, where.value
 
 

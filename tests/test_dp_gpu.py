@@ -9,7 +9,9 @@ all-reduces and replayed.  Three models: MLP 3072->1024->1024->10 (per-call
 (bucket reduce-scatter, each rank updates half the parameters, all-gather of
 the new weights at the next step's start), and the same split-form model
 with bucket all-reduces, its first-layer bucket reduced in row chunks as the
-chunks are computed.  Needs two visible GPUs (skipped otherwise).
+chunks are computed.  The collectives go through the library's NCCL stubs
+(moonbit_nccl_*), and once more through torch.distributed for the last
+model.  Needs two visible GPUs (skipped otherwise).
 """
 from __future__ import annotations
 
@@ -36,6 +38,7 @@ def _free_port():
 
 
 def _problem(model):
+    model = model.replace("_torch", "")
     import sys
     sys.path.insert(0, ROOT)
     from moonxi_net_b200 import synthetic
@@ -73,8 +76,13 @@ def _worker(rank, world, port, outdir, use_graph, model):
         lo, hi = nn.shard_rows(512, rank, world)
         X = torch.from_numpy(x[lo:hi].copy()).to(dev)
         Y = torch.from_numpy(y[lo:hi].copy()).to(dev)
+        torch_coll = model.endswith("_torch")
+        model = model.replace("_torch", "")
         m = nn.MLP(dims, w, b, precision="3xtf32", process_group=dist.group.WORLD,
-                   shard_update=(model != "split_allreduce"))
+                   shard_update=(model != "split_allreduce"),
+                   collectives="torch" if torch_coll else None)
+        from moonxi_net_b200.collectives import NcclCollectives
+        assert isinstance(m.coll, NcclCollectives) != torch_coll
         assert m.fused == (model != "mlp3072")
         assert m.sharded == (model == "split")
         m.last_bucket_chunks = 4  # exercise the chunked first-layer bucket
@@ -90,6 +98,7 @@ def _worker(rank, world, port, outdir, use_graph, model):
                 losses.append(float(m.step(X, Y, 512).item()))
         m.sync_params()  # sharded update: gather every rank's pieces
         torch.cuda.synchronize()
+        m.close()
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), params=_flat_params(m),
                  losses=np.array(losses))
         dist.barrier()
@@ -116,7 +125,8 @@ def _run(use_graph, model):
         return [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
 
 
-@pytest.mark.parametrize("model", ["mlp3072", "split", "split_allreduce"])
+@pytest.mark.parametrize("model", ["mlp3072", "split", "split_allreduce",
+                                   "split_allreduce_torch"])
 @pytest.mark.parametrize("use_graph", [False, True])
 def test_dp2_matches_single_gpu(cuda_device, use_graph, model):
     from moonxi_net_b200 import nn

@@ -6,8 +6,9 @@ up itself (the reference GPU backend runs everything out of one bump pool),
 or a process under a fixed memory budget.  This entry point serves them: its
 scratch is a fixed 64 MiB array inside the library.  These tests call it
 through the C ABI and hold it to the regular 3xTF32 entry point (mx_gemm_ex)
-on the same inputs, for two different problems in a row, so stale scratch
-contents from the previous call would show.  This file is named to run last.
+on the same inputs, and to an fp64 evaluation of the same expression, for
+two different problems in a row, so stale scratch contents from the previous
+call would show.  This file is named to run last.
 """
 from __future__ import annotations
 
@@ -44,6 +45,13 @@ def _scale(a, b, M, K, N, ta, tb, alpha, beta, c0, bias):
         bias.double().abs()[None, :]
 
 
+def _fp64(a, b, bias, c0, M, K, N, ta, tb, alpha, beta, relu):
+    A = a.double().t() if ta else a.double()
+    B = b.double().t() if tb else b.double()
+    c = alpha * (A @ B) + beta * c0.double() + bias.double()[None, :]
+    return torch.clamp_min(c, 0.0) if relu else c
+
+
 def _regular(a, b, bias, c0, M, K, N, ta, tb, alpha, beta, relu):
     c = c0.clone()
     rc = _lib.lib().mx_gemm_ex(None, a.data_ptr(), b.data_ptr(), c.data_ptr(), bias.data_ptr(),
@@ -76,6 +84,9 @@ def test_noalloc_matches_regular_entry_point_two_calls(cuda_device, ta, tb):
         scale = _scale(a, b, M, K, N, ta, tb, alpha, beta, c0, bias)
         err = float(((got.double() - want.double()).abs() / scale).max())
         assert err <= _tol(K), (M, K, N, err)
+        exact = _fp64(a, b, bias, c0, M, K, N, ta, tb, alpha, beta, relu)
+        err64 = float(((got.double() - exact).abs() / scale).max())
+        assert err64 <= _tol(K), (M, K, N, err64)
     assert status.tolist() == [0, 0]
 
 
@@ -105,3 +116,18 @@ def test_noalloc_rejects_problems_beyond_its_scratch(cuda_device):
     assert rc == _lib.MX_ERR_UNSUPPORTED
     torch.cuda.synchronize()
     assert bool((c == 7.0).all())  # nothing was launched
+
+
+def test_noalloc_status_word_reads_clear(cuda_device):
+    """Calls without a dev_status report through the library's own word,
+    which mx_noalloc_status reads and clears; after good calls it is zero."""
+    import ctypes
+    M, K, N = 256, 384, 512
+    a, b, bias, c0 = _problem(M, K, N, 1, 0, 31)
+    got = _noalloc(a, b, bias, c0, M, K, N, 1, 0, 1.0, 0.0, 1)
+    where = ctypes.c_int32(-1)
+    assert _lib.lib().mx_noalloc_status(ctypes.byref(where)) == _lib.MX_OK
+    assert where.value == 0
+    exact = _fp64(a, b, bias, c0, M, K, N, 1, 0, 1.0, 0.0, 1)
+    scale = _scale(a, b, M, K, N, 1, 0, 1.0, 0.0, c0, bias)
+    assert float(((got.double() - exact).abs() / scale).max()) <= _tol(K)

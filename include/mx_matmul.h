@@ -131,6 +131,25 @@ int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo, int
                          const float* bias, int32_t relu, const float* mask, int64_t ldm,
                          int32_t passes, int32_t flags, void* stream);
 
+/* mx_gemm_split_ex that also writes colsum[N] = the sums over the M rows of
+ * the stored output (after bias, ReLU and mask).  When the output is a
+ * layer's dY -- the dX GEMM of the layer above, masked by this layer's ReLU --
+ * these are the layer's bias gradient: reduce_sum_to on the tape
+ * (moonxi-net/grad/grad.mbt:163-174, moonxi-net-gpu/tensor/
+ * trait_impl.mbt:85-133), which the reference runs as a separate kernel
+ * (cuda_kernels.cu:1383-1406), fused into the GEMM's epilogue.  Deterministic
+ * (fixed summation order).  scratch: mx_gemm_colsum_scratch_bytes(M, N)
+ * bytes of device memory owned by the caller, 256-byte aligned, not shared
+ * with a call that overlaps this one. */
+int32_t mx_gemm_split_colsum_ex(void* handle, const float* a_hi, const float* a_lo, int64_t lda,
+                                int32_t a_kmajor, const float* b_hi, const float* b_lo,
+                                int64_t ldb, int32_t b_kmajor, float* c, float* c_hi, float* c_lo,
+                                int64_t ldc, int32_t M, int32_t K, int32_t N, float alpha,
+                                float beta, const float* bias, int32_t relu, const float* mask,
+                                int64_t ldm, int32_t passes, int32_t flags, float* colsum,
+                                void* scratch, uint64_t scratch_bytes, void* stream);
+uint64_t mx_gemm_colsum_scratch_bytes(int32_t M, int32_t N);
+
 /* Allocation-free 3xTF32 GEMM.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory inside a library call --
  * for example a host runtime that reserved its whole device-memory budget up
@@ -257,6 +276,20 @@ int32_t mx_softmax_ce_labels_split(void* handle, const float* logits, const floa
                                    float* grad, float* g_hi, float* g_lo, float* loss,
                                    int32_t batch, int32_t num_classes, int32_t denom,
                                    void* stream);
+
+/* mx_softmax_ce_labels_split that also writes colsum[num_classes] = the
+ * column sums of the gradient: the output layer's bias gradient
+ * (reduce_sum_to, grad/grad.mbt:163-174; cuda_kernels.cu:1383-1406 in the
+ * reference), fused into the loss kernel, deterministic.  scratch:
+ * mx_softmax_ce_colsum_scratch_bytes(batch, num_classes) bytes of caller
+ * device memory, 256-byte aligned (0 bytes: num_classes above 4096, not
+ * fused; the call then returns MX_ERR_UNSUPPORTED). */
+int32_t mx_softmax_ce_labels_split_colsum(void* handle, const float* logits, const float* labels,
+                                          float* grad, float* g_hi, float* g_lo, float* loss,
+                                          int32_t batch, int32_t num_classes, int32_t denom,
+                                          float* colsum, void* scratch, uint64_t scratch_bytes,
+                                          void* stream);
+uint64_t mx_softmax_ce_colsum_scratch_bytes(int32_t batch, int32_t num_classes);
 
 /* mx_sgd_momentum_autoclip that also writes the split copy p_hi/p_lo of the
  * updated parameters (same flat layout) for the next step's GEMMs. */

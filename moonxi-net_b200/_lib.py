@@ -59,6 +59,13 @@ SIGNATURES = {
                                 _i32, _vp]),
     "mx_softmax_ce_labels_split": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                           _vp]),
+    "mx_gemm_split_colsum_ex": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i32, _vp,
+                                       _vp, _vp, _i64, _i32, _i32, _i32, _f32, _f32, _vp, _i32,
+                                       _vp, _i64, _i32, _i32, _vp, _vp, ctypes.c_uint64, _vp]),
+    "mx_gemm_colsum_scratch_bytes": (ctypes.c_uint64, [_i32, _i32]),
+    "mx_softmax_ce_labels_split_colsum": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
+                                                 _i32, _vp, _vp, ctypes.c_uint64, _vp]),
+    "mx_softmax_ce_colsum_scratch_bytes": (ctypes.c_uint64, [_i32, _i32]),
     "mx_sgd_momentum_autoclip_split": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32,
                                               _vp, _vp, _vp, _vp]),
     "mx_gemm_3xtf32_noalloc":(_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,

@@ -364,13 +364,13 @@ MX_EXPORT int32_t mx_split_tf32(void* handle, const float* src, int32_t rows, in
   return finish(ctx, split_tf32(ctx, src, ld, rows, cols, hi, lo, ld_out, s), s);
 }
 
-MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo,
-                                   int64_t lda, int32_t a_kmajor, const float* b_hi,
-                                   const float* b_lo, int64_t ldb, int32_t b_kmajor, float* c,
-                                   float* c_hi, float* c_lo, int64_t ldc, int32_t M, int32_t K,
-                                   int32_t N, float alpha, float beta, const float* bias,
-                                   int32_t relu, const float* mask, int64_t ldm, int32_t passes,
-                                   int32_t flags, void* stream) {
+namespace {
+int gemm_split(void* handle, const float* a_hi, const float* a_lo, int64_t lda, int32_t a_kmajor,
+               const float* b_hi, const float* b_lo, int64_t ldb, int32_t b_kmajor, float* c,
+               float* c_hi, float* c_lo, int64_t ldc, int32_t M, int32_t K, int32_t N,
+               float alpha, float beta, const float* bias, int32_t relu, const float* mask,
+               int64_t ldm, int32_t passes, int32_t flags, float* colsum, void* scratch,
+               uint64_t scratch_bytes, void* stream) {
   Scoped scope(handle);
   Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
@@ -380,7 +380,7 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
   if (!c_hi && c_lo) return MX_ERR_INVALID;
   TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
   L.sched = ctx->sched;
-  const size_t sk = tc_streamk_bytes(M, N, K, ctx->num_sms);
+  const size_t sk = tc_streamk_bytes(M, N, K, ctx->num_sms, passes);
   if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
     L.ws = ctx->workspace;
     L.ws_bytes = ctx->ws_bytes;
@@ -390,8 +390,41 @@ MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float*
   TcEpilogue E;
   E.c = c; E.ldc = ldc; E.alpha = alpha; E.beta = beta; E.bias = bias; E.relu = relu ? 1 : 0;
   E.mask = mask; E.ldm = ldm; E.c_hi = c_hi; E.c_lo = c_lo;
+  E.colsum = colsum; E.colsum_scratch = scratch; E.colsum_scratch_bytes = scratch_bytes;
   cudaStream_t s = pick_stream(ctx, stream);
   return finish(ctx, tc_gemm_split(L, A, B, E, M, N, K, passes, s), s);
+}
+}  // namespace
+
+MX_EXPORT int32_t mx_gemm_split_ex(void* handle, const float* a_hi, const float* a_lo,
+                                   int64_t lda, int32_t a_kmajor, const float* b_hi,
+                                   const float* b_lo, int64_t ldb, int32_t b_kmajor, float* c,
+                                   float* c_hi, float* c_lo, int64_t ldc, int32_t M, int32_t K,
+                                   int32_t N, float alpha, float beta, const float* bias,
+                                   int32_t relu, const float* mask, int64_t ldm, int32_t passes,
+                                   int32_t flags, void* stream) {
+  return gemm_split(handle, a_hi, a_lo, lda, a_kmajor, b_hi, b_lo, ldb, b_kmajor, c, c_hi, c_lo,
+                    ldc, M, K, N, alpha, beta, bias, relu, mask, ldm, passes, flags, nullptr,
+                    nullptr, 0, stream);
+}
+
+MX_EXPORT int32_t mx_gemm_split_colsum_ex(void* handle, const float* a_hi, const float* a_lo,
+                                          int64_t lda, int32_t a_kmajor, const float* b_hi,
+                                          const float* b_lo, int64_t ldb, int32_t b_kmajor,
+                                          float* c, float* c_hi, float* c_lo, int64_t ldc,
+                                          int32_t M, int32_t K, int32_t N, float alpha,
+                                          float beta, const float* bias, int32_t relu,
+                                          const float* mask, int64_t ldm, int32_t passes,
+                                          int32_t flags, float* colsum, void* scratch,
+                                          uint64_t scratch_bytes, void* stream) {
+  if (!colsum) return MX_ERR_INVALID;
+  return gemm_split(handle, a_hi, a_lo, lda, a_kmajor, b_hi, b_lo, ldb, b_kmajor, c, c_hi, c_lo,
+                    ldc, M, K, N, alpha, beta, bias, relu, mask, ldm, passes, flags, colsum,
+                    scratch, scratch_bytes, stream);
+}
+
+MX_EXPORT uint64_t mx_gemm_colsum_scratch_bytes(int32_t M, int32_t N) {
+  return tc_colsum_scratch_bytes(M, N);
 }
 
 MX_EXPORT int32_t moonbit_cuda_set_device(int32_t device) {
@@ -471,9 +504,10 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
   if (!c || M <= 0 || N <= 0 || K < 0) return 0;
   GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
   const int p = resolve_precision(c, M, K, N, precision);
-  const size_t sk = tc_streamk_bytes(M, N, K, c->num_sms);
-  if (p == MX_PREC_3XTF32) return tc_gemm_workspace_bytes(g, 3) + sk;
-  if (p == MX_PREC_TF32) return tc_gemm_workspace_bytes(g, 1) + sk;
+  if (p == MX_PREC_3XTF32)
+    return tc_gemm_workspace_bytes(g, 3) + tc_streamk_bytes(M, N, K, c->num_sms, 3);
+  if (p == MX_PREC_TF32)
+    return tc_gemm_workspace_bytes(g, 1) + tc_streamk_bytes(M, N, K, c->num_sms, 1);
   if (p == MX_PREC_NPARRAY) return 0;  // no split-K in NpArray order
   return simt_gemm_scratch_bytes(c, g);
 }
@@ -565,6 +599,30 @@ MX_EXPORT int32_t mx_softmax_ce_labels_split(void* handle, const float* logits,
   return finish(c, softmax_ce_labels(c, logits, labels, grad, loss, batch, num_classes, denom, s,
                                      g_hi, g_lo),
                 s);
+}
+
+MX_EXPORT int32_t mx_softmax_ce_labels_split_colsum(void* handle, const float* logits,
+                                                    const float* labels, float* grad,
+                                                    float* g_hi, float* g_lo, float* loss,
+                                                    int32_t batch, int32_t num_classes,
+                                                    int32_t denom, float* colsum, void* scratch,
+                                                    uint64_t scratch_bytes, void* stream) {
+  Scoped scope(handle);
+  Context* c = scope.c;
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (!logits || !labels || !grad || !g_hi || !g_lo || !colsum || batch <= 0 ||
+      num_classes <= 0 || denom <= 0)
+    return MX_ERR_INVALID;
+  if (c->precision == MX_PREC_NPARRAY) return MX_ERR_UNSUPPORTED;  // split form is the fast path
+  cudaStream_t s = pick_stream(c, stream);
+  return finish(c,
+                softmax_ce_labels_colsum(c, logits, labels, grad, loss, batch, num_classes, denom,
+                                         s, g_hi, g_lo, colsum, scratch, scratch_bytes),
+                s);
+}
+
+MX_EXPORT uint64_t mx_softmax_ce_colsum_scratch_bytes(int32_t batch, int32_t num_classes) {
+  return softmax_ce_colsum_scratch_bytes(batch, num_classes);
 }
 
 MX_EXPORT int32_t mx_sgd_momentum_autoclip_split(void* handle, float* params, const float* grads,

@@ -674,6 +674,7 @@ void plan_splits(const Context* ctx, const GemmArgs& g, int* splits, int* kb_per
 }  // namespace
 
 size_t simt_gemm_scratch_bytes(const Context* ctx, const GemmArgs& g) {
+  if (skinny_applies(g)) return skinny_scratch_bytes(ctx, g);
   int sp, kps;
   plan_splits(ctx, g, &sp, &kps);
   return sp > 1 ? static_cast<size_t>(sp) * g.M * g.N * sizeof(float) : 0;
@@ -742,6 +743,7 @@ int simt_gemm(Context* ctx, const GemmArgs& g, cudaStream_t s) {
     int rc = ensure_workspace(ctx, need);
     if (rc != kOk) return rc;
   }
+  if (skinny_applies(g)) return skinny_gemm(ctx, g, s, ctx->workspace, ctx->ws_bytes);
   return simt_gemm_launch(ctx, g, s, static_cast<float*>(ctx->workspace), ctx->ws_bytes);
 }
 

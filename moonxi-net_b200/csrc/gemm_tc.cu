@@ -82,14 +82,48 @@ struct TcParams {
   int relu;
   uint64_t timeout_ns;
   bool a_map3d, b_map3d;  // MN-major operand loaded by one 3-D copy per tile
-  // Stream-K: the (tile, k-block) iterations are split evenly over the CTAs;
-  // a tile shared by several CTAs is summed by whichever finishes last.
+  // Split tiles.  sk = 1 (stream-K): the (tile, k-block) iterations of the
+  // tiles from sk_tile0 on are split evenly over the CTAs.  sk = 2 (tail
+  // split): after the full data-parallel waves, each of the tail_r remaining
+  // tiles keeps a primary CTA for k-blocks [0, tail_kp) and the idle CTAs
+  // ("helpers") take the rest -- tail_s pieces of tail_len k-blocks per tile
+  // when there are at least as many helpers as tiles, else whole tails of
+  // several tiles each (at most tail_j per helper), all helpers walking k in
+  // step.  Either way a tile shared by several CTAs is summed, in k order, by
+  // whichever finishes last.
   int sk;
-  int sk_tile0;           // first tile of the stream-K region
-  float* sk_partials;     // [2 * gridDim.x][128][256] fp32 partial tiles
+  int sk_tile0;           // first tile of the split region
+  int tail_r, tail_kp, tail_s, tail_len, tail_j;
+  float* sk_partials;     // partial tiles: [slots][128][256] fp32
   int* sk_counters;       // [num_tiles] arrival counters, zero at launch
   int* tile_counter;      // dynamic whole-tile scheduling (zero at launch), or null
+  // Column sums of the stored output (the bias gradient of the layer whose
+  // dY this GEMM produces): colsum[col] = sum over rows < M of the stored
+  // value.  Each tile's sums go to colsum_part[tm][col]; the last tile of an
+  // N-tile column to finish (arrival counter colsum_cnt[tn], zero at launch
+  // and left zero) adds the M-tiles' rows in order.  Null: off.
+  float* colsum;
+  float* colsum_part;     // [tiles_m][N]
+  int* colsum_cnt;        // [tiles_n]
 };
+
+// Column sums of a warp's 32 x 32 block (lane = row, x[j] = column j):
+// afterwards x[0] of lane l holds the sum over the 32 rows of column l.
+// Butterfly reduce-scatter: at each step a lane keeps the half of its
+// columns selected by its lane bit and adds the partner's copy of that half
+// (31 shuffles for 32 columns).  Fixed order: deterministic.
+__device__ __forceinline__ void warp_colsum32(float (&x)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? x[i] : x[i + o];
+      const float keep = upper ? x[i + o] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+}
 
 // Grouped raster: bands of 16 M-tiles, N-major inside a band, so the CTAs
 // running at one time share A and B tiles in L2.
@@ -127,13 +161,15 @@ struct SegIter {
   int64_t g, g_end;  // stream-K iteration cursor
   int t;             // static data-parallel tile cursor
   int n;             // dynamic: tiles taken from the ring so far
+  int u;             // tail split: segments taken so far
   bool dp_done;
   __device__ __forceinline__ void init(const TcParams& p, int num_kb) {
     t = blockIdx.x;
     n = 0;
+    u = 0;
     dp_done = false;
     g = g_end = 0;
-    if (p.sk) {
+    if (p.sk == 1) {
       const int64_t base = static_cast<int64_t>(p.sk_tile0) * num_kb;
       const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
       g = base + W * blockIdx.x / gridDim.x;
@@ -170,6 +206,34 @@ struct SegIter {
     }
     return r;
   }
+  // Tail split: this CTA's next segment of the remainder tiles (see TcParams).
+  __device__ __forceinline__ bool next_tail(const TcParams& p, int num_kb, int& tile, int& kb0,
+                                            int& kb1) {
+    const int r = p.tail_r, c = blockIdx.x;
+    if (c < r) {  // primary of remainder tile c
+      if (u++ > 0) return false;
+      tile = p.sk_tile0 + c;
+      kb0 = 0;
+      kb1 = p.tail_kp;
+      return true;
+    }
+    const int h = c - r, H = gridDim.x - r;
+    if (p.tail_s > 0) {  // one piece of one tail
+      if (u++ > 0 || h >= r * p.tail_s) return false;
+      const int piece = h / r;
+      tile = p.sk_tile0 + h % r;
+      kb0 = p.tail_kp + piece * p.tail_len;
+      kb1 = piece == p.tail_s - 1 ? num_kb : kb0 + p.tail_len;
+      return true;
+    }
+    const int i = h + u * H;  // whole tails of tiles h, h + H, ...
+    if (i >= r) return false;
+    ++u;
+    tile = p.sk_tile0 + i;
+    kb0 = p.tail_kp;
+    kb1 = num_kb;
+    return true;
+  }
   template <int ROLE>
   __device__ __forceinline__ bool next(const TcParams& p, int num_kb, int& tile, int& kb0,
                                        int& kb1, const TileRing& ring, volatile int* abort_flag) {
@@ -184,6 +248,7 @@ struct SegIter {
       dp_done = true;
       if (*abort_flag) return false;
     }
+    if (p.sk == 2) return next_tail(p, num_kb, tile, kb0, kb1);
     if (g >= g_end) return false;
     tile = static_cast<int>(g / num_kb);
     kb0 = static_cast<int>(g - static_cast<int64_t>(tile) * num_kb);
@@ -202,11 +267,54 @@ __device__ __forceinline__ int sk_cta_of(int64_t g, int64_t W, int G) {
 }
 __device__ __forceinline__ int64_t sk_start(int c, int64_t W, int G) { return W * c / G; }
 
+// Partial-tile slots of both split modes (index into p.sk_partials, in
+// kBM x kBN tiles).  own_slot: where this CTA parks its part of tile t;
+// tile_parts / part_slot: how many parts tile t has and where its j-th part
+// in k order lies (the finisher's view).
+__device__ __forceinline__ int64_t own_slot(const TcParams& p, int t, int num_kb) {
+  if (p.sk == 1) {
+    const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
+    const int64_t tile_g0 = static_cast<int64_t>(t - p.sk_tile0) * num_kb;
+    return static_cast<int64_t>(blockIdx.x) * 2 +
+           (sk_start(blockIdx.x, W, gridDim.x) >= tile_g0 ? 0 : 1);
+  }
+  const int r = p.tail_r, c = blockIdx.x;
+  if (c < r) return c;
+  const int h = c - r;
+  if (p.tail_s > 0) return r + h;
+  const int H = gridDim.x - r;
+  return r + static_cast<int64_t>(h) * p.tail_j + (t - p.sk_tile0 - h) / H;
+}
+__device__ __forceinline__ int tile_parts(const TcParams& p, int t, int num_kb, int& c_first) {
+  if (p.sk == 1) {
+    const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
+    const int64_t tile_g0 = static_cast<int64_t>(t - p.sk_tile0) * num_kb;
+    c_first = sk_cta_of(tile_g0, W, gridDim.x);
+    return sk_cta_of(tile_g0 + num_kb - 1, W, gridDim.x) - c_first + 1;
+  }
+  c_first = 0;
+  return 1 + (p.tail_s > 0 ? p.tail_s : 1);
+}
+__device__ __forceinline__ int64_t part_slot(const TcParams& p, int t, int num_kb, int c_first,
+                                             int j) {
+  if (p.sk == 1) {
+    const int c = c_first + j;
+    const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
+    const int64_t tile_g0 = static_cast<int64_t>(t - p.sk_tile0) * num_kb;
+    return static_cast<int64_t>(c) * 2 + (sk_start(c, W, gridDim.x) >= tile_g0 ? 0 : 1);
+  }
+  const int r = p.tail_r, i = t - p.sk_tile0;
+  if (j == 0) return i;                                                  // the primary
+  if (p.tail_s > 0) return r + static_cast<int64_t>(j - 1) * r + i;      // piece j - 1
+  const int H = gridDim.x - r;
+  return r + static_cast<int64_t>(i % H) * p.tail_j + i / H;            // the helper's tail
+}
+
 // Epilogue of one 32-column chunk of one output row: v holds alpha-less
 // accumulator values; applies alpha/beta/bias/ReLU/mask, stores c and the
 // hi/lo split.
 __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0,
-                                            const float (&acc)[32], bool vec_ok, bool mask_vec) {
+                                            float (&acc)[32], bool vec_ok, bool mask_vec) {
   const int64_t roff = static_cast<int64_t>(row) * p.ldc;
   const bool full_chunk = col0 + 32 <= p.N;
   float v[32];
@@ -276,12 +384,14 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
         }
     }
   }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) acc[j] = v[j];  // the stored values, for column sums
 }
 
 // Epilogue of four consecutive outputs (row, col..col+3): the same math as
 // store_chunk for a 4-wide group.
-__device__ __forceinline__ void store_quad(const TcParams& p, int row, int col, float4 acc,
-                                           bool vec_ok, bool mask_vec) {
+__device__ __forceinline__ float4 store_quad(const TcParams& p, int row, int col, float4 acc,
+                                             bool vec_ok, bool mask_vec) {
   const int64_t roff = static_cast<int64_t>(row) * p.ldc;
   const bool full = col + 4 <= p.N;
   float v[4] = {acc.x, acc.y, acc.z, acc.w};
@@ -323,6 +433,7 @@ __device__ __forceinline__ void store_quad(const TcParams& p, int row, int col, 
       }
   }
   (void)mask_vec;
+  return make_float4(v[0], v[1], v[2], v[3]);  // the stored values, for column sums
 }
 
 __device__ __forceinline__ void epilogue_bar() {
@@ -533,10 +644,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           reinterpret_cast<uintptr_t>(p.c_lo)) & 15u) == 0;
     const bool mask_vec = (p.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0);
     __shared__ int sk_last;  // broadcast of the arrival test among the epilogue warps
-    const int64_t sk_base = static_cast<int64_t>(p.sk_tile0) * num_kb;  // first SK iteration
-    const int64_t W = static_cast<int64_t>(p.num_tiles - p.sk_tile0) * num_kb;
-    const int G = gridDim.x;
-    const int64_t my_start = p.sk ? sk_start(blockIdx.x, W, G) : 0;  // relative to sk_base
+    __shared__ int cs_last;
+    __shared__ float cs_warp[4][kBN];  // column sums of parts of the tile's rows
+    // The tile's column sums into colsum_part[tm] (value(c) for the tile's
+    // column c), then the arrival test of its N-tile column: the last M-tile
+    // to arrive adds every M-tile's row in order (the result does not depend
+    // on which tile arrives last).  All four epilogue warps call it.
+    auto colsum_commit = [&](int tm, int tn, auto value) {
+      epilogue_bar();
+      const int c_base = tn * kBN;
+#pragma unroll
+      for (int c = row_in_tile; c < kBN; c += 128) {
+        const int col = c_base + c;
+        if (col < p.N) p.colsum_part[static_cast<int64_t>(tm) * p.N + col] = value(c);
+      }
+      __threadfence();
+      epilogue_bar();
+      if (row_in_tile == 0) {
+        const int old = atomicAdd(&p.colsum_cnt[tn], 1);
+        cs_last = (old == p.tiles_m - 1) ? 1 : 0;
+        if (cs_last) p.colsum_cnt[tn] = 0;  // ready for the next launch
+      }
+      epilogue_bar();
+      if (cs_last) {
+        __threadfence();
+#pragma unroll
+        for (int c = row_in_tile; c < kBN; c += 128) {
+          const int col = c_base + c;
+          if (col < p.N) {
+            const float* src = p.colsum_part + col;
+            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+            int m = 0;
+            for (; m + 4 <= p.tiles_m; m += 4) {  // four independent chains
+              s0 += __ldcg(src + static_cast<int64_t>(m) * p.N);
+              s1 += __ldcg(src + static_cast<int64_t>(m + 1) * p.N);
+              s2 += __ldcg(src + static_cast<int64_t>(m + 2) * p.N);
+              s3 += __ldcg(src + static_cast<int64_t>(m + 3) * p.N);
+            }
+            for (; m < p.tiles_m; ++m) s0 += __ldcg(src + static_cast<int64_t>(m) * p.N);
+            p.colsum[col] = (s0 + s1) + (s2 + s3);
+          }
+        }
+      }
+    };
     int local = 0;
     SegIter it;
     it.init(p, num_kb);
@@ -551,14 +701,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int row = tm * kBM + row_in_tile;
       const bool whole = kb0 == 0 && kb1 == num_kb;
-      // partial tile: this CTA's slot (0: its share starts inside this tile)
+      // partial tile: this CTA's slot
       float* slot = nullptr;
-      if (!whole) {
-        const int64_t tile_g0 = static_cast<int64_t>(t) * num_kb - sk_base;
-        const int sel = my_start >= tile_g0 ? 0 : 1;
-        slot = p.sk_partials + (static_cast<int64_t>(blockIdx.x) * 2 + sel) * (kBM * kBN) +
+      if (!whole)
+        slot = p.sk_partials + own_slot(p, t, num_kb) * (kBM * kBN) +
                static_cast<int64_t>(row_in_tile) * kBN;
-      }
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         uint32_t r[32];
@@ -569,11 +716,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if (whole) {
           const int col0 = tn * kBN + chunk * 32;
-          if (row < p.M && col0 < p.N) {
-            float a[32];
+          const bool live = row < p.M && col0 < p.N;
+          float a[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) a[j] = __uint_as_float(r[j]);
-            store_chunk(p, row, col0, a, vec_ok, mask_vec);
+          for (int j = 0; j < 32; ++j) a[j] = __uint_as_float(r[j]);
+          if (live) store_chunk(p, row, col0, a, vec_ok, mask_vec);
+          if (p.colsum) {  // whole warp: rows past M and columns past N add zero
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = (live && col0 + j < p.N) ? a[j] : 0.0f;
+            warp_colsum32(a, lane);
+            cs_warp[lane_grp][chunk * 32 + lane] = a[0];
           }
         } else {
 #pragma unroll
@@ -585,18 +737,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       bar_arrive(&acc_empty[acc]);  // TMEM is free again; partials are in memory
+      if (whole && p.colsum)
+        colsum_commit(tm, tn, [&](int c) {
+          return (cs_warp[0][c] + cs_warp[1][c]) + (cs_warp[2][c] + cs_warp[3][c]);
+        });
       if (!whole) {
         // Arrival: the last CTA to finish its part of tile t sums all parts
         // (in k order, so the result does not depend on who is last) and runs
         // the epilogue.  Nobody waits for anybody.
-        const int64_t tile_g0 = static_cast<int64_t>(t) * num_kb - sk_base;
-        const int c_first = sk_cta_of(tile_g0, W, G);
-        const int c_last = sk_cta_of(tile_g0 + num_kb - 1, W, G);
+        int c_first = 0;
+        const int parts = tile_parts(p, t, num_kb, c_first);
         __threadfence();
         epilogue_bar();
         if (row_in_tile == 0) {
           const int old = atomicAdd(&p.sk_counters[t], 1);
-          sk_last = (old == c_last - c_first) ? 1 : 0;
+          sk_last = (old == parts - 1) ? 1 : 0;
           if (sk_last) p.sk_counters[t] = 0;  // ready for the next launch
         }
         epilogue_bar();
@@ -608,14 +763,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int q = row_in_tile & 63;
           const int64_t tile_off = static_cast<int64_t>(row_in_tile >> 6) * kBN + q * 4;
           const int col = tn * kBN + q * 4;
+          float4 cs = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // column sums of my rows
 #pragma unroll 1
           for (int i0 = 0; i0 < kBM / 2; i0 += 8) {
             float4 s[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) s[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int c = c_first; c <= c_last; ++c) {  // k order: same sum on any finisher
-              const int sel = sk_start(c, W, G) >= tile_g0 ? 0 : 1;
-              const float* src = p.sk_partials + (static_cast<int64_t>(c) * 2 + sel) * (kBM * kBN) +
+            for (int j = 0; j < parts; ++j) {  // k order: same sum on any finisher
+              const float* src = p.sk_partials + part_slot(p, t, num_kb, c_first, j) * (kBM * kBN) +
                                  tile_off + static_cast<int64_t>(i0) * 2 * kBN;
               float4 v[8];
 #pragma unroll
@@ -632,8 +787,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int r = tm * kBM + (row_in_tile >> 6) + 2 * (i0 + u);
-              if (r < p.M && col < p.N) store_quad(p, r, col, s[u], vec_ok, mask_vec);
+              if (r < p.M && col < p.N) {
+                const float4 o = store_quad(p, r, col, s[u], vec_ok, mask_vec);
+                cs.x += o.x;
+                cs.y += col + 1 < p.N ? o.y : 0.0f;
+                cs.z += col + 2 < p.N ? o.z : 0.0f;
+                cs.w += col + 3 < p.N ? o.w : 0.0f;
+              }
             }
+          }
+          if (p.colsum) {
+            // the two row halves' sums, then the tile's commit
+            *reinterpret_cast<float4*>(&cs_warp[row_in_tile >> 6][q * 4]) = cs;
+            colsum_commit(tm, tn, [&](int c) { return cs_warp[0][c] + cs_warp[1][c]; });
           }
         }
       }
@@ -827,6 +993,75 @@ size_t kmajor_split_bytes(const GemmArgs& g, int passes) {
                    align256(static_cast<size_t>(g.N) * kp * 4));
 }
 
+// How the tiles of a GEMM are split across the CTAs (see TcParams::sk).
+struct SplitPlan {
+  int mode = 0;           // 0: whole tiles only, 1: stream-K, 2: tail split
+  int tile0 = 0;          // first split tile
+  int r = 0, kp = 0, s = 0, len = 0, j = 0;  // tail split
+  size_t slots = 0;       // partial tiles of scratch
+};
+
+SplitPlan plan_split(int M, int N, int K, int num_sms, int passes) {
+  static const bool disabled = [] {
+    const char* e = std::getenv("MX_STREAMK");
+    return e && e[0] == '0';
+  }();
+  static const bool tail_enabled = [] {
+    const char* e = std::getenv("MX_TAILSPLIT");
+    return !(e && e[0] == '0');
+  }();
+  SplitPlan sp;
+  if (disabled || M <= 0 || N <= 0 || K <= 0 || num_sms <= 0) return sp;
+  const int bk = passes == 1 ? 32 : kBK;
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int num_kb = (K + bk - 1) / bk;
+  const int waves = (tiles + num_sms - 1) / num_sms;
+  const double fill = static_cast<double>(tiles) / (static_cast<double>(waves) * num_sms);
+  const int rem = tiles % num_sms;
+  // Stream-K when whole tiles leave most SMs idle (e.g. the 32 tiles of a
+  // 1000-wide output layer): its CTAs walk k at staggered offsets, which
+  // costs L2 reuse, so only there.  Each CTA's share is at least 8 k-blocks.
+  if (fill < 0.5) {
+    if (static_cast<int64_t>(rem) * num_kb < 8LL * num_sms) return sp;
+    sp.mode = 1;
+    sp.tile0 = (tiles / num_sms) * num_sms;
+    sp.slots = static_cast<size_t>(2) * num_sms;
+    return sp;
+  }
+  // Tail split of a part-filled last wave (e.g. the 128 tiles of a 1024-row
+  // layer on 148 SMs, or the 68 left after three waves of 148): the
+  // remainder tiles' primaries take k-blocks [0, kp), the idle CTAs the
+  // rest, in step with one another.
+  if (!tail_enabled || rem == 0 || num_kb < 16) return sp;
+  const int r = rem, H = num_sms - r;
+  int kp, s = 0, len = 0, j = 0, helper_load;
+  if (H >= r) {  // pieces: each tail cut in s pieces, one helper each
+    s = std::max(1, std::min(H / r, num_kb / 8));
+    kp = num_kb / (s + 1);
+    len = (num_kb - kp) / s;
+    helper_load = num_kb - kp - (s - 1) * len;
+  } else {       // whole tails, j per helper
+    j = (r + H - 1) / H;
+    kp = static_cast<int>((static_cast<int64_t>(num_kb) * j + j / 2) / (j + 1));
+    helper_load = j * (num_kb - kp);
+  }
+  if (kp < 1 || kp >= num_kb || (s > 0 && len < 1)) return sp;
+  // worth it only if the last wave gets clearly shorter (partial tiles cost
+  // a write and a read of 128 KB each)
+  const int last = std::max(kp, helper_load);
+  if (last > num_kb * 9 / 10) return sp;
+  sp.mode = 2;
+  sp.tile0 = tiles - r;
+  sp.r = r;
+  sp.kp = kp;
+  sp.s = s;
+  sp.len = len;
+  sp.j = j;
+  sp.slots = s > 0 ? static_cast<size_t>(r) + static_cast<size_t>(r) * s
+                   : static_cast<size_t>(r) + static_cast<size_t>(H) * j;
+  return sp;
+}
+
 int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
                   const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s) {
   if (M == 0 || N == 0) return kOk;
@@ -857,6 +1092,16 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   p.timeout_ns = L.timeout_ns;
   p.a_map3d = !A.kmajor && (M % 32 == 0 || A.padded);
   p.b_map3d = !B.kmajor && (N % 32 == 0 || B.padded);
+  if (E.colsum) {
+    if (!E.colsum_scratch || E.colsum_scratch_bytes < tc_colsum_scratch_bytes(M, N))
+      return kErrInvalid;
+    p.colsum = E.colsum;
+    p.colsum_part = static_cast<float*>(E.colsum_scratch);
+    p.colsum_cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(E.colsum_scratch) +
+                                          align256(sizeof(float) * p.tiles_m * N));
+    cudaError_t me = cudaMemsetAsync(p.colsum_cnt, 0, sizeof(int) * p.tiles_n, s);
+    if (me != cudaSuccess) return cuda_status(me);
+  }
   // Fewest CTAs that still finish the tiles in the same number of waves: a
   // 128- or 512-tile GEMM takes 128 SMs, leaving the rest to a concurrent
   // NCCL all-reduce at no cost to the GEMM (B200 has 148 SMs).
@@ -871,13 +1116,19 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
     cudaError_t me = cudaMemsetAsync(L.sched, 0, sizeof(int), s);
     if (me != cudaSuccess) return cuda_status(me);
   }
-  const size_t sk_need = tc_streamk_bytes(M, N, K, L.num_sms);
-  if (sk_need > 0 && L.ws && L.ws_bytes >= sk_need) {
-    p.sk = 1;
-    p.sk_tile0 = (p.num_tiles / L.num_sms) * L.num_sms;  // full waves stay data-parallel
+  const SplitPlan sp = plan_split(M, N, K, L.num_sms, passes);
+  const size_t sk_need = tc_streamk_bytes(M, N, K, L.num_sms, passes);
+  if (sp.mode != 0 && L.ws && L.ws_bytes >= sk_need && !p.tile_counter) {
+    p.sk = sp.mode;
+    p.sk_tile0 = sp.tile0;  // full waves stay data-parallel
+    p.tail_r = sp.r;
+    p.tail_kp = sp.kp;
+    p.tail_s = sp.s;
+    p.tail_len = sp.len;
+    p.tail_j = sp.j;
     p.sk_partials = static_cast<float*>(L.ws);
     p.sk_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(L.ws) +
-                                           static_cast<size_t>(2) * L.num_sms * kBM * kBN * 4);
+                                           sp.slots * kBM * kBN * 4);
     grid = L.num_sms;
     cudaError_t me = cudaMemsetAsync(p.sk_counters, 0, sizeof(int) * p.num_tiles, s);
     if (me != cudaSuccess) return cuda_status(me);
@@ -888,23 +1139,17 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   return e == cudaSuccess ? kOk : cuda_status(e);
 }
 
-size_t tc_streamk_bytes(int M, int N, int K, int num_sms) {
-  static const bool disabled = [] {
-    const char* e = std::getenv("MX_STREAMK");
-    return e && e[0] == '0';
-  }();
-  if (disabled || M <= 0 || N <= 0 || K <= 0 || num_sms <= 0) return 0;
+size_t tc_colsum_scratch_bytes(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  const size_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
+  return align256(sizeof(float) * tiles_m * N) + align256(sizeof(int) * tiles_n);
+}
+
+size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes) {
+  const SplitPlan sp = plan_split(M, N, K, num_sms, passes);
+  if (sp.mode == 0) return 0;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int num_kb = (K + kBK - 1) / kBK;
-  const int waves = (tiles + num_sms - 1) / num_sms;
-  const double fill = static_cast<double>(tiles) / (static_cast<double>(waves) * num_sms);
-  // Stream-K only pays when whole tiles leave most SMs idle: its CTAs walk
-  // k at staggered offsets, which costs L2 reuse (measured on B200: a
-  // 128-tile GEMM on 148 SMs runs faster data-parallel, a 32-tile one faster
-  // stream-K).  Also each CTA's share must be at least 8 k-blocks.
-  const int rem = tiles % num_sms;
-  if (fill >= 0.5 || static_cast<int64_t>(rem) * num_kb < 8LL * num_sms) return 0;
-  return static_cast<size_t>(2) * num_sms * kBM * kBN * 4 + align256(sizeof(int) * tiles);
+  return sp.slots * kBM * kBN * 4 + align256(sizeof(int) * tiles);
 }
 
 int split_tf32(Context* ctx, const float* src, int64_t ld, int rows, int cols, float* hi,
@@ -920,7 +1165,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (passes != 1 && passes != 3) return kErrInvalid;
   const CopyShape ca = copy_shape(g.ta == 0, g.M, g.K), cb = copy_shape(g.tb != 0, g.N, g.K);
   const size_t split_bytes = tc_gemm_workspace_bytes(g, passes);
-  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->num_sms);
+  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->num_sms, passes);
   int rc = ensure_workspace(ctx, split_bytes + sk_bytes);
   if (rc != kOk) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);

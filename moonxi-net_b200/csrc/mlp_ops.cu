@@ -189,6 +189,112 @@ __global__ void softmax_ce_kernel(const float* __restrict__ logits,
   }
 }
 
+// softmax_ce_kernel that also produces the column sums of the gradient,
+// colsum[j] = sum_b grad[b, j] (the output layer's bias gradient,
+// reduce_sum_to of grad/grad.mbt:163-174, which the reference runs as a
+// separate kernel, cuda_kernels.cu:1383-1406).  Each block stages its 8
+// gradient rows in shared memory ([8][C]) and writes their sum (fixed order)
+// to part[block]; the last block of each group of 32 to arrive adds the
+// group's rows in order into part2[group]; the last group adds the groups in
+// order into colsum.  The result does not depend on arrival order.  Counters
+// cnt[groups + 1] are zero at launch and left zero.
+constexpr int kCeGroup = 32;
+
+__global__ void softmax_ce_colsum_kernel(const float* __restrict__ logits,
+                                         const float* __restrict__ labels,
+                                         float* __restrict__ grad, float* __restrict__ g_hi,
+                                         float* __restrict__ g_lo, float* __restrict__ partial,
+                                         int batch, int C, float denom, int* __restrict__ status,
+                                         float* __restrict__ colsum, float* __restrict__ part,
+                                         float* __restrict__ part2, int* __restrict__ cnt) {
+  extern __shared__ float rows_s[];  // [8][C]
+  __shared__ float row_loss[8];
+  __shared__ int last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  float* my_row = rows_s + warp * C;
+  float loss = 0.0f;
+  if (b < batch) {
+    const float* row = logits + static_cast<int64_t>(b) * C;
+    const int label = checked_label(labels[b], C, status, 303);
+    float mx_ = -INFINITY;
+    for (int j = lane; j < C; j += 32) mx_ = fmaxf(mx_, row[j]);
+    mx_ = warp_max(mx_);
+    float se = 0.0f;
+    for (int j = lane; j < C; j += 32)
+      se = __fadd_rn(se, static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))));
+    se = warp_sum(se);
+    const float lse = static_cast<float>(log(static_cast<double>(se)));
+    if (lane == 0)
+      loss = label >= 0 ? -__fsub_rn(__fsub_rn(row[label], mx_), lse) : __int_as_float(0x7fc00000);
+    float* g = grad + static_cast<int64_t>(b) * C;
+    for (int j = lane; j < C; j += 32) {
+      const float sm =
+          __fdiv_rn(static_cast<float>(exp(static_cast<double>(__fsub_rn(row[j], mx_)))), se);
+      const float gv = __fdiv_rn(__fsub_rn(sm, (j == label) ? 1.0f : 0.0f), denom);
+      g[j] = gv;
+      my_row[j] = gv;
+      if (g_hi) {
+        const int64_t o = static_cast<int64_t>(b) * C + j;
+        const float h = __uint_as_float(f32_to_tf32_rna(gv));
+        g_hi[o] = h;
+        g_lo[o] = __uint_as_float(f32_to_tf32_rna(gv - h));
+      }
+    }
+  } else {
+    for (int j = lane; j < C; j += 32) my_row[j] = 0.0f;
+  }
+  if (lane == 0) row_loss[warp] = loss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int w = 0; w < 8; ++w) s = __fadd_rn(s, row_loss[w]);
+    partial[blockIdx.x] = s;
+  }
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += rows_s[w * C + j];
+    part[static_cast<int64_t>(blockIdx.x) * C + j] = s;
+  }
+  // level 1: the group's last block adds the group's partial rows
+  const int group = blockIdx.x / kCeGroup;
+  const int g0 = group * kCeGroup;
+  const int gn = min(kCeGroup, static_cast<int>(gridDim.x) - g0);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(&cnt[group], 1);
+    last = old == gn - 1;
+    if (last) cnt[group] = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float s = 0.0f;
+    for (int r = g0; r < g0 + gn; ++r) s += __ldcg(part + static_cast<int64_t>(r) * C + j);
+    part2[static_cast<int64_t>(group) * C + j] = s;
+  }
+  // level 2: the last group adds the groups' rows
+  const int groups = (gridDim.x + kCeGroup - 1) / kCeGroup;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(&cnt[groups], 1);
+    last = old == groups - 1;
+    if (last) cnt[groups] = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float s = 0.0f;
+    for (int r = 0; r < groups; ++r) s += __ldcg(part2 + static_cast<int64_t>(r) * C + j);
+    colsum[j] = s;
+  }
+}
+
 // Sums n partials in a fixed order with one block, then
 // mode 0: out[0] = sum / denom;  1: out[0] = sqrt(sum);  2: out[0] += sum.
 __global__ void finish_sum_kernel(const float* __restrict__ partial, int n, float denom,
@@ -442,6 +548,57 @@ int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, fl
                                            static_cast<float>(denom), ctx->status);
   note_launches(1);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e);
+  if (loss) {
+    finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, static_cast<float>(denom), loss, 0);
+    note_launches(1);
+    e = cudaGetLastError();
+  }
+  return cuda_status(e);
+}
+
+// Largest class count the fused column sums stage in shared memory ([8][C]).
+constexpr int kCeColsumMaxC = 4096;
+
+size_t softmax_ce_colsum_scratch_bytes(int batch, int C) {
+  if (batch <= 0 || C <= 0 || C > kCeColsumMaxC) return 0;
+  const size_t blocks = (batch + 7) / 8;
+  const size_t groups = (blocks + kCeGroup - 1) / kCeGroup;
+  auto a256 = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  return a256(blocks * C * sizeof(float)) + a256(groups * C * sizeof(float)) +
+         a256((groups + 1) * sizeof(int));
+}
+
+int softmax_ce_labels_colsum(Context* ctx, const float* logits, const float* labels, float* grad,
+                             float* loss, int batch, int C, int denom, cudaStream_t s,
+                             float* g_hi, float* g_lo, float* colsum, void* scratch,
+                             size_t scratch_bytes) {
+  if (batch <= 0 || C <= 0 || !grad || !colsum) return kErrInvalid;
+  if (C > kCeColsumMaxC) return kErrUnsupported;
+  if (!scratch || scratch_bytes < softmax_ce_colsum_scratch_bytes(batch, C)) return kErrInvalid;
+  const int blocks = (batch + 7) / 8;
+  const int groups = (blocks + kCeGroup - 1) / kCeGroup;
+  auto a256 = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  uint8_t* w = static_cast<uint8_t*>(scratch);
+  float* part = reinterpret_cast<float*>(w);
+  w += a256(static_cast<size_t>(blocks) * C * sizeof(float));
+  float* part2 = reinterpret_cast<float*>(w);
+  w += a256(static_cast<size_t>(groups) * C * sizeof(float));
+  int* cnt = reinterpret_cast<int*>(w);
+  int rc = ensure_small_scratch(ctx, static_cast<size_t>(blocks) * sizeof(float));
+  if (rc != kOk) return rc;
+  float* partial = static_cast<float*>(ctx->small_scratch);
+  cudaError_t e = cudaMemsetAsync(cnt, 0, sizeof(int) * (groups + 1), s);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int smem = 8 * C * static_cast<int>(sizeof(float));
+  static SmemOptIn opt_in;
+  e = opt_in.ensure(softmax_ce_colsum_kernel, 8 * kCeColsumMaxC * static_cast<int>(sizeof(float)));
+  if (e != cudaSuccess) return cuda_status(e);
+  softmax_ce_colsum_kernel<<<blocks, 256, smem, s>>>(logits, labels, grad, g_hi, g_lo, partial,
+                                                     batch, C, static_cast<float>(denom),
+                                                     ctx->status, colsum, part, part2, cnt);
+  note_launches(1);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e);
   if (loss) {
     finish_sum_kernel<<<1, 256, 0, s>>>(partial, blocks, static_cast<float>(denom), loss, 0);

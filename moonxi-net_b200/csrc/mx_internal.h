@@ -62,6 +62,13 @@ int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scr
 // Bytes of split-K scratch simt_gemm would use for this shape on this device.
 size_t simt_gemm_scratch_bytes(const Context* ctx, const GemmArgs& g);
 
+// Exact-fp32 GEMM for skinny shapes (min(M, N) <= 64, gemm_skinny.cu): streams
+// the big operand once.  simt_gemm dispatches to it whenever it applies.
+bool skinny_applies(const GemmArgs& g);
+size_t skinny_scratch_bytes(const Context* ctx, const GemmArgs& g);
+int skinny_gemm(Context* ctx, const GemmArgs& g, cudaStream_t s, void* scratch,
+                size_t scratch_bytes);
+
 // tcgen05 tensor-core GEMM.  passes = 3: 3xTF32 split (fp32-class);
 // passes = 1: plain TF32.  Uses ctx workspace for the split operands.
 int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s);
@@ -81,9 +88,9 @@ struct TcLaunch {
   // launch stream), or null for a static tile order
   int* sched = nullptr;
 };
-// Scratch a stream-K launch of this shape needs (0: whole tiles already
-// fill the machine, no stream-K).
-size_t tc_streamk_bytes(int M, int N, int K, int num_sms);
+// Scratch of the partial tiles a launch of this shape splits (stream-K or
+// tail split; 0: whole tiles only).
+size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes);
 // One operand in hi/lo split form (lo may be null for passes = 1).
 // kmajor: element (r, k) at hi[r * ld + k]; else at hi[k * ld + r].
 struct SplitOperand {
@@ -109,7 +116,14 @@ struct TcEpilogue {
   int64_t ldm = 0;
   float* c_hi = nullptr;
   float* c_lo = nullptr;
+  // optional column sums of the stored output over its M rows (the bias
+  // gradient when the output is a layer's dY); scratch of
+  // tc_colsum_scratch_bytes(M, N) bytes, 256-byte aligned
+  float* colsum = nullptr;
+  void* colsum_scratch = nullptr;
+  size_t colsum_scratch_bytes = 0;
 };
+size_t tc_colsum_scratch_bytes(int M, int N);
 int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
                   const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s);
 // hi/lo split of a row-major [rows][cols] matrix (leading dimension ld) into
@@ -127,6 +141,14 @@ int reduce_sum_leading(Context* ctx, const float* in, float* out, int cols, int 
 int softmax_ce_labels(Context* ctx, const float* logits, const float* labels, float* grad,
                       float* loss, int batch, int C, int denom, cudaStream_t s,
                       float* g_hi = nullptr, float* g_lo = nullptr);
+// softmax_ce_labels that also writes colsum[C] = column sums of the gradient
+// (the output layer's bias gradient), fused; scratch of
+// softmax_ce_colsum_scratch_bytes(batch, C) bytes (0: C too large to fuse).
+size_t softmax_ce_colsum_scratch_bytes(int batch, int C);
+int softmax_ce_labels_colsum(Context* ctx, const float* logits, const float* labels, float* grad,
+                             float* loss, int batch, int C, int denom, cudaStream_t s,
+                             float* g_hi, float* g_lo, float* colsum, void* scratch,
+                             size_t scratch_bytes);
 int sgd_momentum_autoclip(Context* ctx, float* p, const float* g, float* v, int64_t n, float lr,
                           float momentum, float wd, float max_norm, float* norm_out,
                           cudaStream_t s, float* p_hi = nullptr, float* p_lo = nullptr);

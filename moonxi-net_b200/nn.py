@@ -327,12 +327,20 @@ class MLP:
                 bufs = bufs + ([pair(self.dims[0])] + [pair(self.dims[i + 1])
                                                       for i in range(self.L - 1)],
                                [pair(self.dims[i + 1]) for i in range(self.L)])
+                # scratch of the fused bias-gradient column sums (the CE
+                # kernel's and the dX epilogues'; they run one after another
+                # on the step's stream, so one buffer serves all)
+                need = [ops.gemm_colsum_scratch_bytes(B, self.dims[i]) for i in range(1, self.L)]
+                ce = ops.softmax_ce_colsum_scratch_bytes(B, self.dims[-1])
+                self._ce_colsum = ce > 0
+                nbytes = max(need + [ce, 256])
+                bufs = bufs + (torch.empty(nbytes // 4 + 64, device=dev, dtype=torch.float32),)
             self._bufs[B] = bufs
         return bufs
 
     # ------------------------------------------------------------------ step
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        acts, _ = self._buffers(x.shape[0])
+        acts = self._buffers(x.shape[0])[0]
         h = x
         for i in range(self.L):
             h = ops.linear(h, self.w[i], self.b[i], relu=(i + 1 < self.L),
@@ -409,7 +417,7 @@ class MLP:
         the CE kernel and the dX GEMM epilogue (which also applies the ReLU
         mask of the layer below), weights by the optimizer.  Same arithmetic
         as the per-call 3xTF32 path, without its per-GEMM prepasses."""
-        acts, gbuf, hsplit, gsplit = self._buffers(B)
+        acts, gbuf, hsplit, gsplit, cs_scratch = self._buffers(B)
         nt = self.layout == "nt"
         ctx = self.ctx
         timer = self.gemm_timer
@@ -456,8 +464,13 @@ class MLP:
                  bias=self.b[i], relu=not last)
         mark("forward")
         gh, gl = gsplit[self.L - 1]
+        # the output layer's bias gradient comes out of the CE kernel, every
+        # other layer's out of the dX epilogue that produces its dY
+        ce_cs = self._ce_colsum
         ops.softmax_ce_labels_split(acts[self.L - 1], labels, gbuf[self.L - 1], gh, gl,
-                                    self.loss_slot, G, ctx=ctx)
+                                    self.loss_slot, G, ctx=ctx,
+                                    colsum=self.gb[self.L - 1] if ce_cs else None,
+                                    colsum_scratch=cs_scratch)
         mark("loss")
         works = []
         for i in reversed(range(self.L)):
@@ -465,7 +478,8 @@ class MLP:
             g = gbuf[i]
             gh, gl = gsplit[i]
             hh, hl = hsplit[i]
-            ops.reduce_sum_leading(g, out=self.gb[i], ctx=ctx)
+            if i == self.L - 1 and not ce_cs:
+                ops.reduce_sum_leading(g, out=self.gb[i], ctx=ctx)
             # dW in row chunks; with a process group, the first layer's bucket
             # (the last one backward produces, nothing left to hide it behind)
             # is all-reduced chunk by chunk as the chunks are computed
@@ -501,7 +515,8 @@ class MLP:
                 gemm(2 * B * fi * fo, a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True,
                      b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=fi if nt else fo,
                      b_kmajor=not nt, M=B, K=fo, N=fi, c=gbuf[i - 1], c_hi=ph, c_lo=pl,
-                     mask=acts[i - 1], ldm=fi)
+                     mask=acts[i - 1], ldm=fi, colsum=self.gb[i - 1],
+                     colsum_scratch=cs_scratch)
         mark("backward")
         for wk in works:
             wk.wait()

@@ -200,27 +200,54 @@ def gemm_split(a_hi, a_lo, lda: int, a_kmajor: bool, b_hi, b_lo, ldb: int, b_kma
                M: int, K: int, N: int, c=None, c_hi=None, c_lo=None, ldc: int | None = None,
                alpha: float = 1.0, beta: float = 0.0, bias=None, relu: bool = False,
                mask=None, ldm: int = 0, passes: int = 3, padded: int = 0, ctx=None,
-               stream=None) -> None:
+               stream=None, colsum=None, colsum_scratch=None) -> None:
     """tcgen05 GEMM on split operands (mx_gemm_split_ex); see the header.
     padded: bit 0 / bit 1 when A / B copies have 32 readable floats past
-    their last row."""
+    their last row.  colsum: also write the column sums of the stored output
+    (mx_gemm_split_colsum_ex; colsum_scratch holds colsum_scratch_bytes)."""
     ref = c if c is not None else c_hi
-    rc = _lib.lib().mx_gemm_split_ex(
-        _handle(ctx, a_hi), a_hi.data_ptr(), _ptr(a_lo), lda, int(a_kmajor), b_hi.data_ptr(),
-        _ptr(b_lo), ldb, int(b_kmajor), _ptr(c), _ptr(c_hi), _ptr(c_lo),
-        N if ldc is None else ldc, M, K, N, float(alpha), float(beta), _ptr(bias), int(relu),
-        _ptr(mask), ldm, passes, int(padded), _stream_ptr(stream))
-    check(rc, "mx_gemm_split_ex")
+    args = (_handle(ctx, a_hi), a_hi.data_ptr(), _ptr(a_lo), lda, int(a_kmajor), b_hi.data_ptr(),
+            _ptr(b_lo), ldb, int(b_kmajor), _ptr(c), _ptr(c_hi), _ptr(c_lo),
+            N if ldc is None else ldc, M, K, N, float(alpha), float(beta), _ptr(bias), int(relu),
+            _ptr(mask), ldm, passes, int(padded))
+    if colsum is None:
+        rc = _lib.lib().mx_gemm_split_ex(*args, _stream_ptr(stream))
+        check(rc, "mx_gemm_split_ex")
+    else:
+        rc = _lib.lib().mx_gemm_split_colsum_ex(
+            *args, colsum.data_ptr(), colsum_scratch.data_ptr(),
+            colsum_scratch.numel() * colsum_scratch.element_size(), _stream_ptr(stream))
+        check(rc, "mx_gemm_split_colsum_ex")
     return ref
 
 
+def gemm_colsum_scratch_bytes(M: int, N: int) -> int:
+    return int(_lib.lib().mx_gemm_colsum_scratch_bytes(M, N))
+
+
+def softmax_ce_colsum_scratch_bytes(batch: int, C: int) -> int:
+    """0 when C is too large for the fused column sums."""
+    return int(_lib.lib().mx_softmax_ce_colsum_scratch_bytes(batch, C))
+
+
 def softmax_ce_labels_split(logits, labels, grad, g_hi, g_lo, loss, denom: int, ctx=None,
-                            stream=None) -> None:
+                            stream=None, colsum=None, colsum_scratch=None) -> None:
+    """CE forward+backward writing the gradient and its split copy; with
+    colsum, also the gradient's column sums (the output layer's bias
+    gradient, mx_softmax_ce_labels_split_colsum)."""
     B, C = logits.shape
-    rc = _lib.lib().mx_softmax_ce_labels_split(
-        _handle(ctx, logits), logits.data_ptr(), labels.data_ptr(), grad.data_ptr(),
-        g_hi.data_ptr(), g_lo.data_ptr(), _ptr(loss), B, C, int(denom), _stream_ptr(stream))
-    check(rc, "mx_softmax_ce_labels_split")
+    if colsum is None:
+        rc = _lib.lib().mx_softmax_ce_labels_split(
+            _handle(ctx, logits), logits.data_ptr(), labels.data_ptr(), grad.data_ptr(),
+            g_hi.data_ptr(), g_lo.data_ptr(), _ptr(loss), B, C, int(denom), _stream_ptr(stream))
+        check(rc, "mx_softmax_ce_labels_split")
+    else:
+        rc = _lib.lib().mx_softmax_ce_labels_split_colsum(
+            _handle(ctx, logits), logits.data_ptr(), labels.data_ptr(), grad.data_ptr(),
+            g_hi.data_ptr(), g_lo.data_ptr(), _ptr(loss), B, C, int(denom), colsum.data_ptr(),
+            colsum_scratch.data_ptr(), colsum_scratch.numel() * colsum_scratch.element_size(),
+            _stream_ptr(stream))
+        check(rc, "mx_softmax_ce_labels_split_colsum")
 
 
 def sgd_momentum_autoclip_split(params, grads, vels, p_hi, p_lo, lr, momentum, weight_decay,

@@ -12,6 +12,9 @@
 * ``mlp784_step.json`` -- loss and gradient checksums of one step of
   configuration "MLP 784->256->10, batch 64, seed 0" from the oracle.
 
+The reference GPU step's curves in ``mlp3072_loss_curve.json`` are added by
+``make_ref_gpu_curve.py`` (needs a GPU); rewriting the curve here drops them.
+
 Run from the repository root:  python tests/golden/make_golden.py [--skip-curve]
 """
 from __future__ import annotations

@@ -108,26 +108,34 @@ def _loss_curve(precision):
         losses[s:s + 1].copy_(m.step(X, Y))
     got = losses.cpu().numpy().astype(np.float64)
     diff = np.abs(got - np.asarray(ref, np.float64))
-    return diff, fx
+    return diff, fx, got
 
 
 def test_mlp3072_loss_curve_nparray_mode(cuda_device):
     """200 steps in NpArray mode: within 1e-4 of the CPU curve at every step
     (the operation order is the CPU path's, so the curves coincide)."""
-    diff, _ = _loss_curve("nparray")
+    diff, _, _ = _loss_curve("nparray")
     assert float(diff.max()) <= 1e-4, (int(diff.argmax()), float(diff.max()))
 
 
 @pytest.mark.parametrize("precision", ["3xtf32", "fp32"])
 def test_mlp3072_loss_curve_fast_modes(cuda_device, precision):
-    """200 steps with the fast kernels.  Any reordering of fp32 sums is
-    amplified by the training dynamics; the fixture records how far a float64
-    run lands from the fp32 NpArray curve.  The fast curves must track the
-    NpArray curve at least that closely (and within 1e-4 when the float64
-    run itself does)."""
-    diff, fx = _loss_curve(precision)
-    bound = max(1e-4, 2.0 * fx["max_abs_dev_fp64_vs_oracle"])
-    assert float(diff.max()) <= bound, (int(diff.argmax()), float(diff.max()), bound)
+    """200 steps with the fast kernels against the NpArray CPU curve.  Any
+    reordering of fp32 sums is amplified by the training dynamics, so the
+    bound is measured on the reference itself: the fixture holds the curves
+    of the reference's own GPU training step (its exported kernels -- cuBLAS
+    cuda_matmul on both of its call paths, its CE, bias-gradient and
+    atomic-sum optimizer kernels -- several runs each,
+    tests/golden/make_ref_gpu_curve.py) and their largest distance from the
+    NpArray curve.  The fast curves must stay within that distance, or within
+    1e-4 if that is larger."""
+    diff, fx, got = _loss_curve(precision)
+    bound = max(1e-4, fx["max_abs_dev_ref_gpu_vs_oracle"])
+    vs_ref_gpu = min(  # distance to the nearest reference GPU curve, reported on failure
+        float(np.abs(got - np.array([struct.unpack("<f", bytes.fromhex(h))[0] for h in c])).max())
+        for c in fx["ref_gpu_curves_hex"].values())
+    assert float(diff.max()) <= bound, (int(diff.argmax()), float(diff.max()), bound,
+                                        vs_ref_gpu)
 
 
 def test_graph_replay_bit_identical(cuda_device):

@@ -86,8 +86,65 @@ def _problem(dims, batch, seed):
     return ws, bs, x, y
 
 
+@pytest.mark.parametrize("padded", [0, 3])
+def test_gemm_split_colsum_is_the_bias_gradient(cuda_device, padded):
+    """The fused column sums equal the fp64 column sums of the stored output
+    (after bias, ReLU and mask, rows past M excluded), are bit-identical run
+    to run, and leave the arrival counters ready for the next launch."""
+    M, K, N = 1000, 392, 300   # partial tiles in both directions
+    g = torch.Generator("cuda").manual_seed(4)
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = torch.randn(K, N, device="cuda", generator=g)
+    mask = torch.randn(M, N, device="cuda", generator=g)
+    ah, al = _split(A.contiguous())
+    bh, bl = _split(B.t().contiguous())
+    c = torch.empty(M, N, device="cuda")
+    scratch = torch.empty(ops.gemm_colsum_scratch_bytes(M, N) // 4, device="cuda")
+    sums = []
+    for _ in range(3):
+        cs = torch.full((N,), float("nan"), device="cuda")
+        ops.gemm_split(ah, al, K, True, bh, bl, K, True, M, K, N, c=c, mask=mask, ldm=N,
+                       padded=padded, colsum=cs, colsum_scratch=scratch)
+        sums.append(cs)
+    torch.cuda.synchronize()
+    want = c.double().sum(0)
+    scale = c.double().abs().sum(0)
+    err = float(((sums[0].double() - want).abs() / scale.clamp_min(1e-30)).max())
+    assert err <= 1e-6 * math.sqrt(M), err
+    assert torch.equal(sums[0], sums[1]) and torch.equal(sums[1], sums[2])
+
+
+def test_softmax_ce_colsum_is_the_bias_gradient(cuda_device):
+    B, C = 1000, 1000   # the last block and the last group are partial
+    g = torch.Generator("cuda").manual_seed(5)
+    logits = torch.randn(B, C, device="cuda", generator=g) * 3
+    labels = torch.randint(0, C, (B,), device="cuda", generator=g).float()
+    grad, gh, gl = (torch.empty(B, C, device="cuda") for _ in range(3))
+    loss = torch.empty(1, device="cuda")
+    scratch = torch.empty(ops.softmax_ce_colsum_scratch_bytes(B, C) // 4, device="cuda")
+    out = []
+    for _ in range(2):
+        cs = torch.full((C,), float("nan"), device="cuda")
+        ops.softmax_ce_labels_split(logits, labels, grad, gh, gl, loss, 4096, colsum=cs,
+                                    colsum_scratch=scratch)
+        out.append(cs)
+    torch.cuda.synchronize()
+    want = grad.double().sum(0)
+    scale = grad.double().abs().sum(0)
+    assert float(((out[0].double() - want).abs() / scale).max()) <= 1e-6 * math.sqrt(B)
+    assert torch.equal(out[0], out[1])
+    p = torch.softmax(logits.double(), 1)
+    ref = (p - torch.nn.functional.one_hot(labels.long(), C).double()) / 4096
+    assert float((grad.double() - ref).abs().max()) <= 1e-9
+    assert ops.softmax_ce_colsum_scratch_bytes(B, 5000) == 0  # too wide to fuse
+
+
 @pytest.mark.parametrize("layout", ["nn", "nt"])
-def test_split_step_bit_identical_to_per_call_3xtf32(cuda_device, layout):
+def test_split_step_matches_per_call_3xtf32(cuda_device, layout):
+    """The split-form step runs the same 3xTF32 GEMMs as the per-call path, so
+    the loss and every weight gradient are bit-identical; its bias gradients
+    come from the fused column sums (another fixed summation order than the
+    separate reduction), so they agree to fp32 rounding of the column sums."""
     dims = [1024, 512, 256, 128]
     ws, bs, x, y = _problem(dims, 384, 7)
     if layout == "nt":
@@ -96,10 +153,58 @@ def test_split_step_bit_identical_to_per_call_3xtf32(cuda_device, layout):
     fused = nn.MLP(dims, ws, bs, layout=layout, precision="3xtf32")
     plain = nn.MLP(dims, ws, bs, layout=layout, precision="3xtf32", fused=False)
     assert fused.fused and not plain.fused
+    lf = fused.step(X, Y, update=False).clone()
+    lp = plain.step(X, Y, update=False).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(lf, lp)
+    gbuf = plain._buffers(384)[1]
+    for i in range(len(dims) - 1):
+        assert torch.equal(fused.gw[i], plain.gw[i])
+        dy = gbuf[i].double()
+        want, scale = dy.sum(0), dy.abs().sum(0).clamp_min(1e-30)
+        for m in (fused, plain):
+            assert float(((m.gb[i].double() - want).abs() / scale).max()) <= 1e-6 * math.sqrt(384)
+    # and the training runs stay together over several steps
     for _ in range(3):
         lf = fused.step(X, Y).clone()
         lp = plain.step(X, Y).clone()
     torch.cuda.synchronize()
-    assert torch.equal(lf, lp)
-    assert torch.equal(fused.params, plain.params)
-    assert torch.equal(fused.grads, plain.grads)
+    assert abs(float(lf) - float(lp)) <= 1e-6
+    rel = float((fused.params - plain.params).norm() / plain.params.norm())
+    assert rel <= 1e-6
+
+
+@pytest.mark.parametrize("M,K,N,a_k,b_k", [
+    (1024, 4096, 4096, True, True),    # 128 tiles on 148 SMs: whole tails, 7 per helper
+    (4096, 1024, 4096, False, False),  # 3 full waves + 68 tiles: one piece per helper
+    (1152, 2048, 2304, True, False),   # 81 tiles on 148 SMs: whole tails, 2 per helper
+])
+def test_tail_split_waves(cuda_device, M, K, N, a_k, b_k):
+    """Shapes whose last wave of tiles is part-filled run the tail split (the
+    remainder tiles' first k-blocks on their own CTAs, the rest on the idle
+    ones, parts summed in k order by the last to finish): fp32-class against
+    fp64, bit-identical run to run, with the fused column sums and mask."""
+    g = torch.Generator("cuda").manual_seed(M + N)
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = torch.randn(K, N, device="cuda", generator=g)
+    mask = torch.randn(M, N, device="cuda", generator=g)
+    bias = torch.randn(N, device="cuda", generator=g)
+    ah, al = _split(A.contiguous() if a_k else A.t().contiguous())
+    bh, bl = _split(B.t().contiguous() if b_k else B.contiguous())
+    scratch = torch.empty(ops.gemm_colsum_scratch_bytes(M, N) // 4, device="cuda")
+    outs = []
+    for _ in range(2):
+        c = torch.empty(M, N, device="cuda")
+        cs = torch.empty(N, device="cuda")
+        ops.gemm_split(ah, al, K if a_k else M, a_k, bh, bl, K if b_k else N, b_k, M, K, N, c=c,
+                       bias=bias, mask=mask, ldm=N, padded=3, colsum=cs, colsum_scratch=scratch)
+        outs.append((c, cs))
+    torch.cuda.synchronize()
+    (c, cs), (c2, cs2) = outs
+    ref = (A.double() @ B.double() + bias.double()[None, :]) * (mask > 0)
+    scale = A.double().abs() @ B.double().abs() + bias.double().abs()[None, :]
+    assert float(((c.double() - ref).abs() / scale).max()) <= 1e-5 * math.sqrt(K)
+    assert torch.equal(c, c2) and torch.equal(cs, cs2)
+    want = c.double().sum(0)
+    assert float(((cs.double() - want).abs() / c.double().abs().sum(0)).max()) <= \
+        1e-6 * math.sqrt(M)

@@ -362,11 +362,45 @@ def square_config_sweep(torch, ops, dev, tf32_peak, fp32_peak):
         "tf32": round(tf32_peak, 1), "fp32_simt": round(fp32_peak, 1)}, "results": rows}
 
 
+def _time_graph(torch, fn, flush, reps=10):
+    """GPU time (s) of one fn() call, host launch overhead excluded: fn is
+    captured in a CUDA graph after an L2 flush (a 256 MB write), R times; the
+    same graph without fn is timed too and subtracted."""
+    fn()  # sizes any workspace before capture
+    torch.cuda.synchronize()
+    graphs = []
+    for with_fn in (True, False):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                flush.zero_()
+                if with_fn:
+                    fn()
+        graphs.append(g)
+    best = []
+    for g in graphs:
+        g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(3):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        best.append(statistics.median(ts))
+    return max(best[0] - best[1], 1e-9) / reps
+
+
 def ragged_config_sweep(torch, ops, dev, hbm_peak, tf32_peak, fp32_peak):
     """BASELINE config "Ragged/skinny GEMMs": M in {1,7,33,127,1000} x K in
     {512,784,3072,4096} x N in {10,100,257,1000}, N(0,1) seed 4, NN/NT/TN,
     bias+ReLU epilogue, the default (AUTO) precision.  M <= 33 is judged on
-    HBM bandwidth (algorithmic bytes 4(MK+KN+MN+N)), the others on TFLOP/s."""
+    HBM bandwidth (algorithmic bytes 4(MK+KN+MN+N)), the others on TFLOP/s.
+    GPU time per call from CUDA-graph replays with L2 flushed before each
+    call (host launch overhead excluded; it dominates the smallest shapes)."""
     from moonxi_net_b200 import synthetic
     flush = torch.empty(int(256e6) // 4, device=dev)
     per_m = {}
@@ -380,9 +414,9 @@ def ragged_config_sweep(torch, ops, dev, hbm_peak, tf32_peak, fp32_peak):
                     b = torch.from_numpy(b_np).to(dev)
                     bias = torch.from_numpy(bias_np).to(dev)
                     c = torch.empty((M, N), device=dev)
-                    t = _time_median(torch, lambda: ops.gemm(a, b, M, K, N, ta=ta, tb=tb,
-                                                             bias=bias, relu=True, out=c),
-                                     flush, reps=7)
+                    t = _time_graph(torch, lambda: ops.gemm(a, b, M, K, N, ta=ta, tb=tb,
+                                                            bias=bias, relu=True, out=c),
+                                    flush)
                     if M <= 33:
                         vals.append(4.0 * (M * K + K * N + M * N + N) / t / 1e9)
                     else:

@@ -94,6 +94,18 @@ int32_t moonbit_cuda_linear_fwd_ex(void* handle, void* x, void* w, void* bias, v
                                    int32_t M, int32_t K, int32_t N, int32_t transpose_w,
                                    int32_t relu, float alpha, void* stream, int32_t precision);
 
+/* The reference's fused forward in its own rounding order:
+ * y = act(bias + sum_k x[m,k] op(w)[k,n]), the sum started from the bias and
+ * accumulated as fp32 multiply then add in k order -- fused_linear_relu /
+ * fused_linear (moonxi-net/nparray/fused_ops.mbt:12-78; weights [out, in],
+ * i.e. transpose_w = 1, there), bit-identical to that CPU code.  pre (may be
+ * NULL) receives the pre-ReLU values, the second result of
+ * fused_linear_relu.  The ordinary forward (moonbit_cuda_linear_fwd) adds
+ * the bias after the rounded matmul (matmul -> add -> relu). */
+int32_t mx_linear_fwd_bias_first(void* handle, const float* x, const float* w, const float* bias,
+                                 float* y, float* pre, int32_t M, int32_t K, int32_t N,
+                                 int32_t transpose_w, int32_t relu, void* stream);
+
 /* General form behind all of the above: C[M,N] = act(alpha op(A) op(B) +
  * beta C + bias[N]) for any transpose flags, explicit leading dimensions
  * (lda/ldb/ldc in elements; 0 = the packed default of cuda_matmul), bias may

@@ -51,6 +51,8 @@ SIGNATURES = {
                                        _f32]),
     "moonbit_cuda_linear_fwd_ex": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                           _i32, _f32, _vp, _i32]),
+    "mx_linear_fwd_bias_first": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+                                        _i32, _vp]),
     "mx_gemm_ex": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _i64,
                           _i64, _f32, _f32, _i32, _vp, _i32]),
     "mx_split_tf32": (_i32, [_vp, _vp, _i32, _i32, _i64, _vp, _vp, _i64, _vp]),

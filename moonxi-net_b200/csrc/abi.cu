@@ -67,6 +67,8 @@ int init_context(Context* c, int device) {
   cudaError_t e = cudaMalloc(&c->status, 4 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(c->status, 0, 4 * sizeof(int));
   c->sched = c->status + 2;
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, Context::kCounters * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, Context::kCounters * sizeof(int));
   if (prev != device) cudaSetDevice(prev);
   return cuda_status(e);
 }
@@ -332,6 +334,28 @@ MX_EXPORT int32_t moonbit_cuda_linear_fwd(void* handle, void* x, void* w, void* 
                                     nullptr, MX_PREC_DEFAULT);
 }
 
+MX_EXPORT int32_t mx_linear_fwd_bias_first(void* handle, const float* x, const float* w,
+                                           const float* bias, float* y, float* pre, int32_t M,
+                                           int32_t K, int32_t N, int32_t transpose_w,
+                                           int32_t relu, void* stream) {
+  Scoped scope(handle);
+  Context* ctx = scope.c;
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  if (!bias || !y) return MX_ERR_INVALID;
+  GemmArgs g = ref_args(const_cast<float*>(x), const_cast<float*>(w), y, M, K, N, 0, transpose_w,
+                        1.0f, 0.0f);
+  g.bias = bias;
+  g.relu = relu ? 1 : 0;
+  g.strict = 1;
+  g.bias_first = 1;
+  g.pre = pre;
+  if (g.M < 0 || g.N < 0 || g.K < 0) return MX_ERR_INVALID;
+  if (g.M == 0 || g.N == 0) return MX_OK;
+  if (g.K > 0 && (!x || !w)) return MX_ERR_INVALID;
+  cudaStream_t s = pick_stream(ctx, stream);
+  return finish(ctx, simt_gemm(ctx, g, s), s);
+}
+
 MX_EXPORT int32_t mx_gemm_ex(void* handle, const float* a, const float* b, float* c,
                              const float* bias, int32_t M, int32_t K, int32_t N,
                              int32_t transpose_a, int32_t transpose_b, int64_t lda, int64_t ldb,
@@ -457,6 +481,7 @@ MX_EXPORT void mx_context_destroy(void* handle) {
   if (c->workspace) cudaFree(c->workspace);
   if (c->small_scratch) cudaFree(c->small_scratch);
   if (c->status) cudaFree(c->status);
+  if (c->counters) cudaFree(c->counters);
   cudaSetDevice(prev);
   delete c;
 }

@@ -81,6 +81,11 @@ struct SimtParams {
   int relu;
   int vec_c;       // C (and bias) allow 16-byte column groups
   uint64_t timeout_ns;
+  // NpArray bias-first order (STRICT only): the sum starts from bias[col]
+  // and the epilogue adds no bias; `pre` (may be null) receives the
+  // pre-ReLU values.
+  int bias_first;
+  float* pre;
 };
 
 // Offset (floats) of element (row, k) inside a K-contiguous [rows][16] tile
@@ -206,6 +211,19 @@ struct StrictAcc {
 #pragma unroll
       for (int j = 0; j < 4 * G; ++j) v[i][j] = 0.0f;
   }
+  // Bias-first order (nparray/fused_ops.mbt:12-78): every sum starts from
+  // the bias of its column.
+  __device__ __forceinline__ void init_bias(const float* bias, int N, int n0, int tx) {
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = n0 + h * 64 + tx * 4 + j;
+        const float b = col < N ? __ldg(bias + col) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i][4 * h + j] = b;
+      }
+  }
   __device__ __forceinline__ float at(int i, int j) const { return v[i][j]; }
   __device__ __forceinline__ void stage(const float* __restrict__ sA,
                                         const float* __restrict__ sB, int ty, int tx) {
@@ -233,12 +251,15 @@ struct AccFor { using type = PackedAcc<BN>; };
 template <int BN>
 struct AccFor<BN, true> { using type = StrictAcc<BN>; };
 
-__device__ __forceinline__ float epi(const SimtParams& p, float acc, float cv, float bv) {
+__device__ __forceinline__ float epi_pre(const SimtParams& p, float acc, float cv, float bv) {
   float v = p.alpha * acc;
   if (p.beta != 0.0f) v = v + p.beta * cv;
-  if (p.bias) v = v + bv;
-  if (p.relu) v = v > 0.0f ? v : 0.0f;
+  if (p.bias && !p.bias_first) v = v + bv;
   return v;
+}
+__device__ __forceinline__ float epi(const SimtParams& p, float acc, float cv, float bv) {
+  const float v = epi_pre(p, acc, cv, bv);
+  return p.relu ? (v > 0.0f ? v : 0.0f) : v;
 }
 
 // The thread's 8 x (BN/16) outputs: rows own_index(ty, i), columns
@@ -288,6 +309,12 @@ __device__ __forceinline__ void store_tile(const SimtParams& p, const Acc& acc, 
         o.z = epi(p, acc.at(i, 4 * h + 2), cv.z, bv.z);
         o.w = epi(p, acc.at(i, 4 * h + 3), cv.w, bv.w);
         *reinterpret_cast<float4*>(crow + col) = o;
+        if (p.pre) {
+          float* prow = p.pre + static_cast<int64_t>(row) * p.ldc;
+          *reinterpret_cast<float4*>(prow + col) = make_float4(
+              epi_pre(p, acc.at(i, 4 * h + 0), cv.x, bv.x), epi_pre(p, acc.at(i, 4 * h + 1), cv.y, bv.y),
+              epi_pre(p, acc.at(i, 4 * h + 2), cv.z, bv.z), epi_pre(p, acc.at(i, 4 * h + 3), cv.w, bv.w));
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -295,6 +322,8 @@ __device__ __forceinline__ void store_tile(const SimtParams& p, const Acc& acc, 
           if (cc >= p.N) continue;
           const float cv = p.beta != 0.0f ? crow[cc] : 0.0f;
           const float bv = p.bias ? __ldg(p.bias + cc) : 0.0f;
+          if (p.pre)
+            p.pre[static_cast<int64_t>(row) * p.ldc + cc] = epi_pre(p, acc.at(i, 4 * h + j), cv, bv);
           crow[cc] = epi(p, acc.at(i, 4 * h + j), cv, bv);
         }
       }
@@ -330,6 +359,9 @@ __global__ void __launch_bounds__(kThreads, Shape<BN>::kCtasPerSm)
 
   typename AccFor<BN, STRICT>::type acc;
   acc.zero();
+  if constexpr (STRICT) {
+    if (p.bias_first) acc.init_bias(p.bias, p.N, n0, tx);
+  }
 
   // Operand tiles of k-block `it` once it has landed (and been transposed).
   auto tile_a = [&](int it) -> const float* {
@@ -689,6 +721,8 @@ int simt_gemm_launch(Context* ctx, const GemmArgs& g, cudaStream_t s, float* scr
   p.M = g.M; p.N = g.N; p.K = g.K;
   p.alpha = g.alpha; p.beta = g.beta; p.relu = g.relu;
   p.timeout_ns = ctx->timeout_ns;
+  p.bias_first = g.strict && g.bias_first && g.bias;
+  p.pre = g.pre;
   plan_splits(ctx, g, &p.splits, &p.kb_per_split);
   if (g.K == 0) { p.splits = 1; p.kb_per_split = 0; }
   if (p.splits > 1) {

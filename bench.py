@@ -335,8 +335,10 @@ def gemm_sweep(torch, ops, peaks, dev, sizes=(8192,)):
 def square_config_sweep(torch, ops, dev, tf32_peak, fp32_peak):
     """BASELINE config "Square fp32 GEMM sweep": M=N=K in 512..8192, NN/NT/TN,
     with and without the bias+ReLU epilogue, N(0,1) entries seed 1, every
-    precision; TFLOP/s (median of 5, L2 flushed) and the fraction of the
-    precision's peak (3xTF32 in TF32-equivalent terms, 3 x 2N^3)."""
+    precision; TFLOP/s (GPU time from CUDA-graph replays, L2 flushed before
+    each call; the per-call path's operand split passes included) and the
+    fraction of the precision's peak (3xTF32 in TF32-equivalent terms,
+    3 x 2N^3)."""
     from moonxi_net_b200 import synthetic
     flush = torch.empty(int(256e6) // 4, device=dev)
     rows = {}
@@ -350,9 +352,9 @@ def square_config_sweep(torch, ops, dev, tf32_peak, fp32_peak):
             for epi in ("plain", "bias_relu"):
                 bv, relu = (bias, True) if epi == "bias_relu" else (None, False)
                 for prec in ("3xtf32", "tf32", "fp32"):
-                    t = _time_median(torch, lambda: ops.gemm(a, b, n, n, n, ta=ta, tb=tb, bias=bv,
-                                                             relu=relu, out=c, precision=prec),
-                                     flush, reps=5 if n >= 2048 else 9)
+                    t = _time_graph(torch, lambda: ops.gemm(a, b, n, n, n, ta=ta, tb=tb, bias=bv,
+                                                            relu=relu, out=c, precision=prec),
+                                    flush, reps=10 if n <= 2048 else 3)
                     tf = 2.0 * n ** 3 / t / 1e12
                     frac = (3 * tf / tf32_peak if prec == "3xtf32" else
                             tf / tf32_peak if prec == "tf32" else tf / fp32_peak)

@@ -222,6 +222,10 @@ void* mx_context_create(int32_t device);
 void mx_context_destroy(void* handle);
 int32_t mx_context_set_stream(void* handle, void* stream);
 int32_t mx_context_set_precision(void* handle, int32_t precision);
+/* SMs this context's tensor-core GEMMs may occupy (0 = all).  A
+ * data-parallel step sets it below the SM count so that collectives
+ * launched on another stream find free SMs while a GEMM runs. */
+int32_t mx_context_set_sm_budget(void* handle, int32_t sms);
 /* Bound (nanoseconds) on every in-kernel wait; default 2 s. */
 int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns);
 /* Pre-sizes the context workspace (split operands, split-K partials) so that

@@ -79,6 +79,7 @@ SIGNATURES = {
     "mx_context_set_stream": (_i32, [_vp, _vp]),
     "mx_context_set_precision": (_i32, [_vp, _i32]),
     "mx_context_set_timeout_ns": (_i32, [_vp, ctypes.c_uint64]),
+    "mx_context_set_sm_budget": (_i32, [_vp, _i32]),
     "mx_context_reserve_workspace": (_i32, [_vp, ctypes.c_uint64]),
     "mx_matmul_workspace_bytes": (ctypes.c_uint64, [_vp, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mx_context_status": (_i32, [_vp, ctypes.POINTER(_i32)]),

@@ -402,9 +402,9 @@ int gemm_split(void* handle, const float* a_hi, const float* a_lo, int64_t lda, 
   if (lda < (a_kmajor ? K : M) || ldb < (b_kmajor ? K : N) || ldc < N) return MX_ERR_INVALID;
   if (mask && ldm < N) return MX_ERR_INVALID;
   if (!c_hi && c_lo) return MX_ERR_INVALID;
-  TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
   L.sched = ctx->sched;
-  const size_t sk = tc_streamk_bytes(M, N, K, ctx->num_sms, passes);
+  const size_t sk = tc_streamk_bytes(M, N, K, ctx->tc_sms(), passes);
   if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
     L.ws = ctx->workspace;
     L.ws_bytes = ctx->ws_bytes;
@@ -512,6 +512,15 @@ MX_EXPORT int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns) {
   return MX_OK;
 }
 
+MX_EXPORT int32_t mx_context_set_sm_budget(void* handle, int32_t sms) {
+  Scoped scope(handle);
+  Context* c = scope.c;
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (sms < 0) return MX_ERR_INVALID;
+  c->sm_budget = sms;
+  return MX_OK;
+}
+
 MX_EXPORT int32_t mx_context_reserve_workspace(void* handle, uint64_t bytes) {
   Scoped scope(handle);
   Context* c = scope.c;
@@ -530,9 +539,9 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
   GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
   const int p = resolve_precision(c, M, K, N, precision);
   if (p == MX_PREC_3XTF32)
-    return tc_gemm_workspace_bytes(g, 3) + tc_streamk_bytes(M, N, K, c->num_sms, 3);
+    return tc_gemm_workspace_bytes(g, 3) + tc_streamk_bytes(M, N, K, c->tc_sms(), 3);
   if (p == MX_PREC_TF32)
-    return tc_gemm_workspace_bytes(g, 1) + tc_streamk_bytes(M, N, K, c->num_sms, 1);
+    return tc_gemm_workspace_bytes(g, 1) + tc_streamk_bytes(M, N, K, c->tc_sms(), 1);
   if (p == MX_PREC_NPARRAY) return 0;  // no split-K in NpArray order
   return simt_gemm_scratch_bytes(c, g);
 }

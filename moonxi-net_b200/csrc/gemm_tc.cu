@@ -1165,7 +1165,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (passes != 1 && passes != 3) return kErrInvalid;
   const CopyShape ca = copy_shape(g.ta == 0, g.M, g.K), cb = copy_shape(g.tb != 0, g.N, g.K);
   const size_t split_bytes = tc_gemm_workspace_bytes(g, passes);
-  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->num_sms, passes);
+  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->tc_sms(), passes);
   int rc = ensure_workspace(ctx, split_bytes + sk_bytes);
   if (rc != kOk) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);
@@ -1188,7 +1188,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   e = cb.kmajor ? launch_split(g.b, g.ldb, true, g.N, g.K, cb.ld, b_hi, b_lo, ctx->num_sms, s)
                 : launch_split(g.b, g.ldb, true, g.K, g.N, cb.ld, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
-  TcLaunch L{ctx->num_sms, ctx->status, ctx->timeout_ns};
+  TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
   L.sched = ctx->sched;
   L.ws = static_cast<uint8_t*>(ctx->workspace) + split_bytes;  // split_bytes is 256-aligned
   L.ws_bytes = sk_bytes;

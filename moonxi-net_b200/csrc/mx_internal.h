@@ -32,6 +32,11 @@ struct Context {
   // no memset.  Calls that overlap on the GPU must not share a context.
   static constexpr int kCounters = 65536;
   int* counters = nullptr;
+  // SMs the tensor-core GEMMs may occupy (0: all).  A data-parallel step
+  // leaves the rest free so that NCCL kernels overlapping a GEMM find SMs
+  // (a persistent GEMM CTA and an NCCL CTA do not fit on one SM together).
+  int sm_budget = 0;
+  int tc_sms() const { return sm_budget > 0 && sm_budget < num_sms ? sm_budget : num_sms; }
 };
 
 // One GEMM as the reference defines it (cuda_kernels.cu:1444-1499), with the

@@ -167,7 +167,8 @@ class MLP:
         # The model's library context carries the precision mode, so the
         # adjacent ops follow it too ("nparray": NpArray operation order).
         self.precision = precision
-        self.ctx = ops.context(self.device.index, precision)
+        # the model's own context: its workspace, status word and SM budget
+        self.ctx = ops.new_context(self.device.index, precision)
         self.lr, self.momentum = float(lr), float(momentum)
         self.weight_decay, self.max_grad_norm = float(weight_decay), float(max_grad_norm)
         self.pg = process_group
@@ -190,6 +191,14 @@ class MLP:
         else:
             self.world = 1
         self._owns_coll = collectives is None and self.coll is not None
+        if self.world > 1:
+            # leave SMs to the collectives that overlap the backward GEMMs: a
+            # persistent GEMM CTA and an NCCL CTA do not fit on one SM together
+            # (on 148 SMs the 128 left also make every power-of-two tile count
+            # a whole number of waves)
+            import os
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            ops.set_sm_budget(self.ctx, sms - int(os.environ.get("MX_COMM_SMS", "20")))
         # Split-form path (3xTF32 with every operand kept as hi/lo copies written
         # by its producer): needs TMA-legal leading dimensions (multiples of 4).
         self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
@@ -447,7 +456,7 @@ class MLP:
         if plan is not None:
             # the new weights: every rank's pieces, layer by layer, on the
             # collective stream while the forward of the earlier layers runs
-            gathers = [plan.all_gather(self._params_full, i, self.coll) for i in range(self.L)]
+            gathers = [self._gather_layer(i) for i in range(self.L)]
         xh, xl = hsplit[0]
         ops.split_tf32(x, xh, xl, ctx=ctx)
         # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
@@ -455,7 +464,8 @@ class MLP:
             last = i + 1 == self.L
             if plan is not None:
                 gathers[i].wait()
-                ops.split_tf32(self.w[i], self.w_hi[i], self.w_lo[i], ctx=ctx)
+                if not self._split_on_coll_stream:
+                    ops.split_tf32(self.w[i], self.w_hi[i], self.w_lo[i], ctx=ctx)
             ah, al = hsplit[i]
             ch, cl = (None, None) if last else hsplit[i + 1]
             gemm(2 * B * d[i] * d[i + 1], a_hi=ah, a_lo=al, lda=d[i], a_kmajor=True,
@@ -531,6 +541,26 @@ class MLP:
         mark("update")
         return self.loss_slot
 
+    @property
+    def _split_on_coll_stream(self):
+        return getattr(self.coll, "stream", None) is not None
+
+    def _gather_layer(self, i):
+        """Sharded update: all-gather layer i's new weights (every rank's
+        pieces) and, where the collectives run on a stream of their own,
+        re-split them to hi/lo right behind the gather on that stream -- the
+        split then runs on the SMs the GEMMs leave free, beside the forward
+        of the earlier layers, instead of in front of layer i's GEMM."""
+        work = self.plan.all_gather(self._params_full, i, self.coll)
+        if not self._split_on_coll_stream:
+            return work
+        from .collectives import _EventWork
+        with torch.cuda.stream(self.coll.stream):
+            ops.split_tf32(self.w[i], self.w_hi[i], self.w_lo[i], ctx=self.ctx)
+            ev = torch.cuda.Event()
+            ev.record(self.coll.stream)
+        return _EventWork(ev)
+
     def _sharded_update(self, update):
         """Global norm from every rank's gradient pieces (one small
         all-reduce that also sums the loss), then the update of this rank's
@@ -578,6 +608,9 @@ class MLP:
         if self.coll is not None and self._owns_coll:
             self.coll.destroy()
         self.coll = None
+        if self.ctx:
+            ops.destroy_context(self.ctx)
+            self.ctx = None
 
 
 class HostBatchPipeline:

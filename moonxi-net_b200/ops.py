@@ -34,6 +34,27 @@ def context(device: int | None = None, mode: str = "default") -> int:
     return h
 
 
+def new_context(device: int, mode: str = "default") -> int:
+    """A context owned by the caller (not shared through `context`); free it
+    with `destroy_context`."""
+    h = _lib.lib().mx_context_create(int(device))
+    if not h:
+        raise _lib.MXError(_lib.MX_ERR_NO_DEVICE, f"mx_context_create({device})")
+    if mode != "default":
+        check(_lib.lib().mx_context_set_precision(h, _prec(mode)), "mx_context_set_precision")
+    return h
+
+
+def destroy_context(h) -> None:
+    if h:
+        _lib.lib().mx_context_destroy(h)
+
+
+def set_sm_budget(ctx, sms: int) -> None:
+    """SMs the context's tensor-core GEMMs may occupy (0 = all)."""
+    check(_lib.lib().mx_context_set_sm_budget(ctx, int(sms)), "mx_context_set_sm_budget")
+
+
 def _handle(ctx, t: torch.Tensor) -> int:
     return ctx if ctx is not None else context(t.device.index)
 

@@ -723,34 +723,39 @@ def run_ours(args):
 
 
 def run_gemm_only(args):
-    """One square GEMM, K timed launches after W warm-ups (L2 flushed between
-    launches); the small case the kernel profiles are taken on."""
+    """One GEMM (square N^3 with --gemm N, or --shape M,K,N), K timed launches
+    after W warm-ups (L2 flushed between launches); the small cases the kernel
+    profiles are taken on."""
     import torch
 
     from moonxi_net_b200 import ops
     torch.cuda.set_device(0)
-    n = args.gemm
+    if args.shape:
+        M, K, N = (int(v) for v in args.shape.split(","))
+    else:
+        M = K = N = args.gemm
     ta, tb = {"nn": (0, 0), "nt": (0, 1), "tn": (1, 0)}[args.layout]
-    a = torch.randn((n, n), device="cuda")
-    b = torch.randn((n, n), device="cuda")
-    c = torch.empty((n, n), device="cuda")
+    a = torch.randn((K, M) if ta else (M, K), device="cuda")
+    b = torch.randn((N, K) if tb else (K, N), device="cuda")
+    c = torch.empty((M, N), device="cuda")
     flush = torch.empty(int(256e6) // 4, device="cuda")
-    prec = "3xtf32" if args.precision == "auto" else args.precision
+    prec = ("3xtf32" if not args.shape else "auto") if args.precision == "auto" else args.precision
     for _ in range(args.warmup):
-        ops.gemm(a, b, n, n, n, ta=ta, tb=tb, out=c, precision=prec)
+        ops.gemm(a, b, M, K, N, ta=ta, tb=tb, out=c, precision=prec)
     times = []
     for _ in range(args.steps):
         flush.zero_()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        ops.gemm(a, b, n, n, n, ta=ta, tb=tb, out=c, precision=prec)
+        ops.gemm(a, b, M, K, N, ta=ta, tb=tb, out=c, precision=prec)
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) / 1e3)
     t = statistics.median(times)
-    print(json.dumps({"metric": f"GEMM {n}^3 {args.layout} TFLOP/s", "precision": prec,
-                      "value": 2.0 * n ** 3 / t / 1e12, "unit": "TFLOP/s", "ms": t * 1e3,
+    by = 4.0 * (M * K + K * N + M * N)
+    print(json.dumps({"metric": f"GEMM {M}x{K}x{N} {args.layout}", "precision": prec,
+                      "tflops": 2.0 * M * N * K / t / 1e12, "gbs": by / t / 1e9, "ms": t * 1e3,
                       "steps": args.steps, "warmup": args.warmup}), flush=True)
     return 0
 
@@ -776,11 +781,13 @@ def main():
     ap.add_argument("--gemm", type=int, default=0, metavar="N",
                     help="time only the square N^3 GEMM of --precision (profiling case)")
     ap.add_argument("--layout", default="nn", choices=["nn", "nt", "tn"])
+    ap.add_argument("--shape", default="", metavar="M,K,N",
+                    help="time only this GEMM (any shape; default precision auto)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps
     if args.impl == "reference":
         return run_reference(args)
-    if args.gemm:
+    if args.gemm or args.shape:
         return run_gemm_only(args)
     return run_ours(args)
 

@@ -357,10 +357,10 @@ SkinnyPlan plan(const Context* ctx, const GemmArgs& g) {
   else if (aligned16(p.b) && p.sbk == 1 && p.sbn % 4 == 0) pl.mode = kSkKVec;
   const int nt = pl.mode == kSkKVec ? kSkThreads : 32 * pl.cpt;
   const int tiles = (p.N + nt - 1) / nt;
-  // enough blocks for about one per SM, each split at least eight stages
-  // deep and at most 16 splits: the last split to arrive reads every split's
-  // partial, so deep split-K trades streaming time for a serial tail
-  const int want = ctx->num_sms;
+  // enough blocks for three per SM (bytes in flight: one block keeps three
+  // 16 KB stages outstanding), each split at least eight stages deep and at
+  // most 16 splits: the last split to arrive reads every split's partial
+  const int want = 3 * ctx->num_sms;
   const int max_splits = std::max(1, std::min(16, p.K / (8 * kSkKT)));
   int splits = std::max(1, std::min(max_splits, (want + tiles - 1) / tiles));
   int kps = (p.K + splits - 1) / splits;

@@ -162,6 +162,56 @@ int32_t mx_gemm_split_colsum_ex(void* handle, const float* a_hi, const float* a_
                                 void* scratch, uint64_t scratch_bytes, void* stream);
 uint64_t mx_gemm_colsum_scratch_bytes(int32_t M, int32_t N);
 
+/* One GEMM of mx_gemm_split_pair: the arguments of mx_gemm_split_colsum_ex
+ * (passes = 3) as a plain struct; colsum = NULL: no column sums. */
+typedef struct mx_split_gemm {
+  const float* a_hi;
+  const float* a_lo;
+  int64_t lda;
+  int32_t a_kmajor;
+  const float* b_hi;
+  const float* b_lo;
+  int64_t ldb;
+  int32_t b_kmajor;
+  float* c;
+  float* c_hi;
+  float* c_lo;
+  int64_t ldc;
+  int32_t M, K, N;
+  float alpha, beta;
+  const float* bias;
+  int32_t relu;
+  const float* mask;
+  int64_t ldm;
+  int32_t flags;
+  float* colsum;
+  void* colsum_scratch;
+  uint64_t colsum_scratch_bytes;
+} mx_split_gemm;
+
+/* Two independent 3xTF32 GEMMs on split operands in one persistent launch:
+ * a Linear layer's backward, dX = dY W^T and dW = X^T dY (grad/blas.mbt:
+ * 35,37), which both read dY and neither reads the other's output.  The
+ * tiles of the GEMM with more k-blocks per tile come first, then the
+ * other's, round robin over the CTAs, so the second GEMM's tiles run their
+ * main loops while the first's epilogues drain: one launch, one prologue and
+ * one unhidden epilogue instead of two.  Every tile is computed whole (no
+ * split of K), so each output equals that of mx_gemm_split_colsum_ex
+ * whenever that call also runs whole tiles.  Layout pairs other than (A
+ * K-major, B either) with (A and B MN-major) run as two launches.  The two
+ * GEMMs' outputs, column-sum scratch and counters must not overlap. */
+int32_t mx_gemm_split_pair(void* handle, const mx_split_gemm* g0, const mx_split_gemm* g1,
+                           void* stream);
+
+/* The work split the tcgen05 GEMM of this context picks for an M x N x K
+ * shape (passes 3 or 1): out[0] = mode (0 whole tiles, 1 stream-K, 2 tail
+ * split), out[1] = first split tile, out[2] = remainder tiles, out[3] =
+ * k-blocks of a remainder tile's primary CTA, out[4] = pieces per tail (tail
+ * split with at least as many idle CTAs as tiles), out[5] = tails per helper
+ * CTA (fewer idle CTAs than tiles).  For tests and tuning. */
+int32_t mx_tc_split_plan(void* handle, int32_t M, int32_t N, int32_t K, int32_t passes,
+                         int32_t* out);
+
 /* Allocation-free 3xTF32 GEMM.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory inside a library call --
  * for example a host runtime that reserved its whole device-memory budget up

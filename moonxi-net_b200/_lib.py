@@ -39,6 +39,18 @@ _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
 _f32 = ctypes.c_float
 
+
+
+class SplitGemm(ctypes.Structure):
+    """mx_split_gemm: one GEMM of mx_gemm_split_pair (include/mx_matmul.h)."""
+    _fields_ = [("a_hi", _vp), ("a_lo", _vp), ("lda", _i64), ("a_kmajor", _i32),
+                ("b_hi", _vp), ("b_lo", _vp), ("ldb", _i64), ("b_kmajor", _i32),
+                ("c", _vp), ("c_hi", _vp), ("c_lo", _vp), ("ldc", _i64),
+                ("M", _i32), ("K", _i32), ("N", _i32), ("alpha", _f32), ("beta", _f32),
+                ("bias", _vp), ("relu", _i32), ("mask", _vp), ("ldm", _i64), ("flags", _i32),
+                ("colsum", _vp), ("colsum_scratch", _vp), ("colsum_scratch_bytes", ctypes.c_uint64)]
+
+
 # name -> (restype, argtypes); mirrors include/mx_matmul.h
 SIGNATURES = {
     "cuda_matmul": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int,
@@ -65,6 +77,8 @@ SIGNATURES = {
                                        _vp, _vp, _i64, _i32, _i32, _i32, _f32, _f32, _vp, _i32,
                                        _vp, _i64, _i32, _i32, _vp, _vp, ctypes.c_uint64, _vp]),
     "mx_gemm_colsum_scratch_bytes": (ctypes.c_uint64, [_i32, _i32]),
+    "mx_gemm_split_pair": (_i32, [_vp, ctypes.POINTER(SplitGemm), ctypes.POINTER(SplitGemm), _vp]),
+    "mx_tc_split_plan": (_i32, [_vp, _i32, _i32, _i32, _i32, ctypes.POINTER(_i32)]),
     "mx_softmax_ce_labels_split_colsum": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                                  _i32, _vp, _vp, ctypes.c_uint64, _vp]),
     "mx_softmax_ce_colsum_scratch_bytes": (ctypes.c_uint64, [_i32, _i32]),

@@ -451,6 +451,63 @@ MX_EXPORT uint64_t mx_gemm_colsum_scratch_bytes(int32_t M, int32_t N) {
   return tc_colsum_scratch_bytes(M, N);
 }
 
+namespace {
+// Argument checks of one GEMM of a pair (those of gemm_split) and its
+// conversion; kOk or MX_ERR_INVALID.
+int pair_gemm(const mx_split_gemm* g, TcPairGemm& out) {
+  if (!g) return MX_ERR_INVALID;
+  if (g->M < 0 || g->N < 0 || g->K < 1) return MX_ERR_INVALID;
+  if (g->lda < (g->a_kmajor ? g->K : g->M) || g->ldb < (g->b_kmajor ? g->K : g->N) ||
+      g->ldc < g->N)
+    return MX_ERR_INVALID;
+  if (g->mask && g->ldm < g->N) return MX_ERR_INVALID;
+  if (!g->c_hi && g->c_lo) return MX_ERR_INVALID;
+  if (g->M > 0 && g->N > 0 && (!g->a_hi || !g->a_lo || !g->b_hi || !g->b_lo))
+    return MX_ERR_INVALID;
+  out.A = SplitOperand{g->a_hi, g->a_lo, g->lda, g->a_kmajor != 0, (g->flags & 1) != 0};
+  out.B = SplitOperand{g->b_hi, g->b_lo, g->ldb, g->b_kmajor != 0, (g->flags & 2) != 0};
+  TcEpilogue& E = out.E;
+  E.c = g->c; E.ldc = g->ldc; E.alpha = g->alpha; E.beta = g->beta; E.bias = g->bias;
+  E.relu = g->relu ? 1 : 0; E.mask = g->mask; E.ldm = g->ldm; E.c_hi = g->c_hi; E.c_lo = g->c_lo;
+  E.colsum = g->colsum; E.colsum_scratch = g->colsum_scratch;
+  E.colsum_scratch_bytes = g->colsum_scratch_bytes;
+  out.M = g->M; out.N = g->N; out.K = g->K;
+  return kOk;
+}
+}  // namespace
+
+MX_EXPORT int32_t mx_gemm_split_pair(void* handle, const mx_split_gemm* g0,
+                                     const mx_split_gemm* g1, void* stream) {
+  Scoped scope(handle);
+  Context* ctx = scope.c;
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  TcPairGemm a, b;
+  int rc = pair_gemm(g0, a);
+  if (rc == kOk) rc = pair_gemm(g1, b);
+  if (rc != kOk) return rc;
+  TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
+  // a layout pair without a paired kernel runs as two launches, which may
+  // split K and then need the stream-K scratch
+  const size_t sk = std::max(tc_streamk_bytes(a.M, a.N, a.K, ctx->tc_sms(), 3),
+                             tc_streamk_bytes(b.M, b.N, b.K, ctx->tc_sms(), 3));
+  if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
+    L.ws = ctx->workspace;
+    L.ws_bytes = ctx->ws_bytes;
+  }
+  cudaStream_t s = pick_stream(ctx, stream);
+  return finish(ctx, tc_gemm_pair(L, a, b, s), s);
+}
+
+MX_EXPORT int32_t mx_tc_split_plan(void* handle, int32_t M, int32_t N, int32_t K, int32_t passes,
+                                   int32_t* out) {
+  Scoped scope(handle);
+  Context* ctx = scope.c;
+  if (!ctx) return MX_ERR_NO_DEVICE;
+  if (!out || M < 1 || N < 1 || K < 1 || (passes != 1 && passes != 3)) return MX_ERR_INVALID;
+  tc_split_plan(M, N, K, ctx->tc_sms(), passes, out);
+  return MX_OK;
+}
+
 MX_EXPORT int32_t moonbit_cuda_set_device(int32_t device) {
   return cuda_status(cudaSetDevice(device));
 }

@@ -105,6 +105,10 @@ struct TcParams {
   float* colsum;
   float* colsum_part;     // [tiles_m][N]
   int* colsum_cnt;        // [tiles_n]
+  // Paired launch (tc_gemm_pair_kernel): the tiles of a second, independent
+  // GEMM follow this one's in the tile order -- pair_tiles of them, whole
+  // tiles only (sk = 0).  0 for a single GEMM.
+  int pair_tiles;
 };
 
 // Column sums of a warp's 32 x 32 block (lane = row, x[j] = column j):
@@ -181,7 +185,7 @@ struct SegIter {
   template <int ROLE>
   __device__ __forceinline__ int next_dp(const TcParams& p, const TileRing& ring,
                                          volatile int* abort_flag) {
-    const int dp_end = p.sk ? p.sk_tile0 : p.num_tiles;
+    const int dp_end = p.sk ? p.sk_tile0 : p.num_tiles + p.pair_tiles;
     if (!p.tile_counter) {
       if (t >= dp_end) return -1;
       const int r = t;
@@ -466,14 +470,67 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int k8) {
   return sdesc_mnmajor(saddr + k8 * kK8MN, BK * 128, kSboMN, kLayoutSw128Base32);
 }
 
-template <int PASSES, bool AK, bool BKM>
-__global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
-                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
-                   const TcParams p) {
-  constexpr int BK = stage_bk<PASSES, AK, BKM>();
+// One stage of operand tiles (A hi/lo, B hi/lo) for k-blocks starting at k0.
+template <int PASSES, bool AK, bool BKM, int BK>
+__device__ __forceinline__ void load_stage(uint8_t* base, const CUtensorMap* ah,
+                                           const CUtensorMap* al, const CUtensorMap* bh,
+                                           const CUtensorMap* bl, uint64_t* bar, int k0, int tm,
+                                           int tn, bool a3d, bool b3d) {
   using C = Cfg<PASSES, BK>;
   constexpr int kATile = C::kATileB, kBTile = C::kBTileB;
+  load_operand<AK, kBM, BK>(base, ah, bar, k0, tm * kBM, a3d);
+  if (PASSES == 3) {
+    load_operand<AK, kBM, BK>(base + kATile, al, bar, k0, tm * kBM, a3d);
+    load_operand<BKM, kBN, BK>(base + 2 * kATile, bh, bar, k0, tn * kBN, b3d);
+    load_operand<BKM, kBN, BK>(base + 2 * kATile + kBTile, bl, bar, k0, tn * kBN, b3d);
+  } else {
+    load_operand<BKM, kBN, BK>(base + kATile, bh, bar, k0, tn * kBN, b3d);
+  }
+}
+
+// The MMAs of one stage: BK/8 slices, three TF32 MMAs per slice for 3xTF32
+// (lo_a.hi_b, hi_a.lo_b, hi_a.hi_b), one for plain TF32.
+template <int PASSES, bool AK, bool BKM, int BK>
+__device__ __forceinline__ void mma_stage(uint32_t s_base, uint32_t d_tmem, uint32_t idesc,
+                                          uint32_t& accumulate) {
+  using C = Cfg<PASSES, BK>;
+  constexpr int kATile = C::kATileB, kBTile = C::kBTileB;
+  const uint32_t s_ah = s_base;
+  const uint32_t s_al = s_base + kATile;
+  const uint32_t s_bh = s_base + (PASSES == 3 ? 2 * kATile : kATile);
+  const uint32_t s_bl = s_base + 2 * kATile + kBTile;
+#pragma unroll
+  for (int k8 = 0; k8 < BK / 8; ++k8) {
+    const uint64_t ah = operand_desc<AK, BK>(s_ah, k8);
+    const uint64_t bh = operand_desc<BKM, BK>(s_bh, k8);
+    if (PASSES == 3) {
+      const uint64_t al = operand_desc<AK, BK>(s_al, k8);
+      const uint64_t bl = operand_desc<BKM, BK>(s_bl, k8);
+      mma_tf32(d_tmem, al, bh, idesc, accumulate);
+      mma_tf32(d_tmem, ah, bl, idesc, 1u);
+      mma_tf32(d_tmem, ah, bh, idesc, 1u);
+    } else {
+      mma_tf32(d_tmem, ah, bh, idesc, accumulate);
+    }
+    accumulate = 1u;
+  }
+}
+
+// The kernel body.  PAIR: a second, independent GEMM (p1, tensor maps *1,
+// operand layouts AK1/BK1) shares the launch; its tiles follow p's in the
+// tile order (whole tiles, static round robin), so a CTA's second tile --
+// typically of the other GEMM -- runs its main loop while the first tile's
+// epilogue drains, and the two GEMMs pay one launch, one prologue and one
+// unhidden epilogue between them.
+template <int PASSES, bool AK, bool BKM, bool PAIR, bool AK1, bool BK1>
+__device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUtensorMap* tmAl,
+                                             const CUtensorMap* tmBh, const CUtensorMap* tmBl,
+                                             const CUtensorMap* tmAh1, const CUtensorMap* tmAl1,
+                                             const CUtensorMap* tmBh1, const CUtensorMap* tmBl1,
+                                             const TcParams& p, const TcParams& p1) {
+  constexpr int BK = stage_bk<PASSES, AK, BKM>();
+  static_assert(!PAIR || stage_bk<PASSES, AK1, BK1>() == BK, "paired GEMMs share the stage shape");
+  using C = Cfg<PASSES, BK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -507,11 +564,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tmAh);
-    tma_prefetch_desc(&tmBh);
+    tma_prefetch_desc(tmAh);
+    tma_prefetch_desc(tmBh);
     if (PASSES == 3) {
-      tma_prefetch_desc(&tmAl);
-      tma_prefetch_desc(&tmBl);
+      tma_prefetch_desc(tmAl);
+      tma_prefetch_desc(tmBl);
+    }
+    if (PAIR) {
+      tma_prefetch_desc(tmAh1);
+      tma_prefetch_desc(tmBh1);
+      tma_prefetch_desc(tmAl1);
+      tma_prefetch_desc(tmBl1);
     }
   }
   if (warp == 1) {
@@ -523,6 +586,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (p.K + BK - 1) / BK;
+  const int num_kb1 = PAIR ? (p1.K + BK - 1) / BK : num_kb;
+  // A segment of the pair's second GEMM: its tile index and k extent.
+  auto second = [&](int& t, int& kb1) {
+    if (PAIR && t >= p.num_tiles) {
+      t -= p.num_tiles;
+      kb1 = num_kb1;
+      return true;
+    }
+    return false;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -537,8 +610,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       it.init(p, num_kb);
       int t, kb0, kb1;
       while (ok && it.next<kProducer>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
+        const bool q1 = second(t, kb1);
+        const TcParams& q = q1 ? p1 : p;
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(t, q.tiles_m, q.tiles_n, tm, tn);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, abort_flag, p.status, p.timeout_ns, 201)) {
             ok = false;
@@ -549,18 +624,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           armed[stage] = true;
           armed_parity[stage] = phase;
           const int k0 = kb * BK;
-          load_operand<AK, kBM, BK>(base, &tmAh, &full[stage], k0, tm * kBM, p.a_map3d);
-          if (PASSES == 3) {
-            load_operand<AK, kBM, BK>(base + kATile, &tmAl, &full[stage], k0, tm * kBM,
-                                      p.a_map3d);
-            load_operand<BKM, kBN, BK>(base + 2 * kATile, &tmBh, &full[stage], k0, tn * kBN,
-                                       p.b_map3d);
-            load_operand<BKM, kBN, BK>(base + 2 * kATile + kBTile, &tmBl, &full[stage], k0,
-                                       tn * kBN, p.b_map3d);
-          } else {
-            load_operand<BKM, kBN, BK>(base + kATile, &tmBh, &full[stage], k0, tn * kBN,
-                                       p.b_map3d);
-          }
+          if (PAIR && q1)
+            load_stage<PASSES, AK1, BK1, BK>(base, tmAh1, tmAl1, tmBh1, tmBl1, &full[stage], k0,
+                                             tm, tn, p1.a_map3d, p1.b_map3d);
+          else
+            load_stage<PASSES, AK, BKM, BK>(base, tmAh, tmAl, tmBh, tmBl, &full[stage], k0, tm,
+                                            tn, p.a_map3d, p.b_map3d);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -575,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(kBM, kBN, !AK, !BKM);
+      const uint32_t idesc0 = idesc_tf32(kBM, kBN, !AK, !BKM);
+      const uint32_t idesc1 = idesc_tf32(kBM, kBN, !AK1, !BK1);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -584,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       it.init(p, num_kb);
       int t, kb0, kb1;
       while (ok && it.next<kMma>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
+        const bool q1 = second(t, kb1);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         ++local;
@@ -601,25 +672,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t s_base = smem_u32(smem + stage * C::kStageBytes);
-          const uint32_t s_ah = s_base;
-          const uint32_t s_al = s_base + kATile;
-          const uint32_t s_bh = s_base + (PASSES == 3 ? 2 * kATile : kATile);
-          const uint32_t s_bl = s_base + 2 * kATile + kBTile;
-#pragma unroll
-          for (int k8 = 0; k8 < BK / 8; ++k8) {
-            const uint64_t ah = operand_desc<AK, BK>(s_ah, k8);
-            const uint64_t bh = operand_desc<BKM, BK>(s_bh, k8);
-            if (PASSES == 3) {
-              const uint64_t al = operand_desc<AK, BK>(s_al, k8);
-              const uint64_t bl = operand_desc<BKM, BK>(s_bl, k8);
-              mma_tf32(d_tmem, al, bh, idesc, accumulate);
-              mma_tf32(d_tmem, ah, bl, idesc, 1u);
-              mma_tf32(d_tmem, ah, bh, idesc, 1u);
-            } else {
-              mma_tf32(d_tmem, ah, bh, idesc, accumulate);
-            }
-            accumulate = 1u;
-          }
+          if (PAIR && q1)
+            mma_stage<PASSES, AK1, BK1, BK>(s_base, d_tmem, idesc1, accumulate);
+          else
+            mma_stage<PASSES, AK, BKM, BK>(s_base, d_tmem, idesc0, accumulate);
           tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
           if (++stage == C::kStages) {
             stage = 0;
@@ -638,11 +694,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int lane_grp = warp & 3;                 // TMEM lanes this warp may access
     const int row_in_tile = lane_grp * 32 + lane;
-    const bool vec_ok =
-        (p.ldc % 4 == 0) &&
-        ((reinterpret_cast<uintptr_t>(p.c) | reinterpret_cast<uintptr_t>(p.c_hi) |
-          reinterpret_cast<uintptr_t>(p.c_lo)) & 15u) == 0;
-    const bool mask_vec = (p.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0);
+    // 16-byte stores of the output / loads of the mask (per GEMM of a pair)
+    auto vec_of = [](const TcParams& q) {
+      return (q.ldc % 4 == 0) &&
+             ((reinterpret_cast<uintptr_t>(q.c) | reinterpret_cast<uintptr_t>(q.c_hi) |
+               reinterpret_cast<uintptr_t>(q.c_lo)) & 15u) == 0;
+    };
+    auto mask_vec_of = [](const TcParams& q) {
+      return (q.ldm % 4 == 0) && ((reinterpret_cast<uintptr_t>(q.mask) & 15u) == 0);
+    };
     __shared__ int sk_last;  // broadcast of the arrival test among the epilogue warps
     __shared__ int cs_last;
     __shared__ __align__(16) float cs_warp[4][kBN];  // column sums of parts of the tile's rows
@@ -650,20 +710,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // column c), then the arrival test of its N-tile column: the last M-tile
     // to arrive adds every M-tile's row in order (the result does not depend
     // on which tile arrives last).  All four epilogue warps call it.
-    auto colsum_commit = [&](int tm, int tn, auto value) {
+    auto colsum_commit = [&](const TcParams& q, int tm, int tn, auto value) {
       epilogue_bar();
       const int c_base = tn * kBN;
 #pragma unroll
       for (int c = row_in_tile; c < kBN; c += 128) {
         const int col = c_base + c;
-        if (col < p.N) p.colsum_part[static_cast<int64_t>(tm) * p.N + col] = value(c);
+        if (col < q.N) q.colsum_part[static_cast<int64_t>(tm) * q.N + col] = value(c);
       }
       __threadfence();
       epilogue_bar();
       if (row_in_tile == 0) {
-        const int old = atomicAdd(&p.colsum_cnt[tn], 1);
-        cs_last = (old == p.tiles_m - 1) ? 1 : 0;
-        if (cs_last) p.colsum_cnt[tn] = 0;  // ready for the next launch
+        const int old = atomicAdd(&q.colsum_cnt[tn], 1);
+        cs_last = (old == q.tiles_m - 1) ? 1 : 0;
+        if (cs_last) q.colsum_cnt[tn] = 0;  // ready for the next launch
       }
       epilogue_bar();
       if (cs_last) {
@@ -671,18 +731,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = row_in_tile; c < kBN; c += 128) {
           const int col = c_base + c;
-          if (col < p.N) {
-            const float* src = p.colsum_part + col;
+          if (col < q.N) {
+            const float* src = q.colsum_part + col;
             float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
             int m = 0;
-            for (; m + 4 <= p.tiles_m; m += 4) {  // four independent chains
-              s0 += __ldcg(src + static_cast<int64_t>(m) * p.N);
-              s1 += __ldcg(src + static_cast<int64_t>(m + 1) * p.N);
-              s2 += __ldcg(src + static_cast<int64_t>(m + 2) * p.N);
-              s3 += __ldcg(src + static_cast<int64_t>(m + 3) * p.N);
+            for (; m + 4 <= q.tiles_m; m += 4) {  // four independent chains
+              s0 += __ldcg(src + static_cast<int64_t>(m) * q.N);
+              s1 += __ldcg(src + static_cast<int64_t>(m + 1) * q.N);
+              s2 += __ldcg(src + static_cast<int64_t>(m + 2) * q.N);
+              s3 += __ldcg(src + static_cast<int64_t>(m + 3) * q.N);
             }
-            for (; m < p.tiles_m; ++m) s0 += __ldcg(src + static_cast<int64_t>(m) * p.N);
-            p.colsum[col] = (s0 + s1) + (s2 + s3);
+            for (; m < q.tiles_m; ++m) s0 += __ldcg(src + static_cast<int64_t>(m) * q.N);
+            q.colsum[col] = (s0 + s1) + (s2 + s3);
           }
         }
       }
@@ -697,10 +757,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++local;
       if (!wait_bar(&acc_full[acc], acc_phase, abort_flag, p.status, p.timeout_ns, 204)) break;
       tc_fence_after();
+      const bool q1 = second(t, kb1);
+      const TcParams& q = q1 ? p1 : p;  // the GEMM of this tile
+      const bool vec_ok = vec_of(q), mask_vec = mask_vec_of(q);
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(t, q.tiles_m, q.tiles_n, tm, tn);
       const int row = tm * kBM + row_in_tile;
-      const bool whole = kb0 == 0 && kb1 == num_kb;
+      const bool whole = q1 || (kb0 == 0 && kb1 == num_kb);
       // partial tile: this CTA's slot
       float* slot = nullptr;
       if (!whole)
@@ -716,14 +779,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if (whole) {
           const int col0 = tn * kBN + chunk * 32;
-          const bool live = row < p.M && col0 < p.N;
+          const bool live = row < q.M && col0 < q.N;
           float a[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) a[j] = __uint_as_float(r[j]);
-          if (live) store_chunk(p, row, col0, a, vec_ok, mask_vec);
-          if (p.colsum) {  // whole warp: rows past M and columns past N add zero
+          if (live) store_chunk(q, row, col0, a, vec_ok, mask_vec);
+          if (q.colsum) {  // whole warp: rows past M and columns past N add zero
 #pragma unroll
-            for (int j = 0; j < 32; ++j) a[j] = (live && col0 + j < p.N) ? a[j] : 0.0f;
+            for (int j = 0; j < 32; ++j) a[j] = (live && col0 + j < q.N) ? a[j] : 0.0f;
             warp_colsum32(a, lane);
             cs_warp[lane_grp][chunk * 32 + lane] = a[0];
           }
@@ -737,8 +800,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       bar_arrive(&acc_empty[acc]);  // TMEM is free again; partials are in memory
-      if (whole && p.colsum)
-        colsum_commit(tm, tn, [&](int c) {
+      if (whole && q.colsum)
+        colsum_commit(q, tm, tn, [&](int c) {
           return (cs_warp[0][c] + cs_warp[1][c]) + (cs_warp[2][c] + cs_warp[3][c]);
         });
       if (!whole) {
@@ -799,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.colsum) {
             // the two row halves' sums, then the tile's commit
             *reinterpret_cast<float4*>(&cs_warp[row_in_tile >> 6][q * 4]) = cs;
-            colsum_commit(tm, tn, [&](int c) { return cs_warp[0][c] + cs_warp[1][c]; });
+            colsum_commit(p, tm, tn, [&](int c) { return cs_warp[0][c] + cs_warp[1][c]; });
           }
         }
       }
@@ -812,6 +875,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+template <int PASSES, bool AK, bool BKM>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                   const TcParams p) {
+  tc_gemm_body<PASSES, AK, BKM, false, AK, BKM>(&tmAh, &tmAl, &tmBh, &tmBl, &tmAh, &tmAl, &tmBh,
+                                                &tmBl, p, p);
+}
+
+// Two independent 3xTF32 GEMMs in one launch (tc_gemm_body, PAIR): p's tiles
+// first, then p1's.
+template <bool AK, bool BKM, bool AK1, bool BK1>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmAh,
+                        const __grid_constant__ CUtensorMap tmAl,
+                        const __grid_constant__ CUtensorMap tmBh,
+                        const __grid_constant__ CUtensorMap tmBl,
+                        const __grid_constant__ CUtensorMap tmAh1,
+                        const __grid_constant__ CUtensorMap tmAl1,
+                        const __grid_constant__ CUtensorMap tmBh1,
+                        const __grid_constant__ CUtensorMap tmBl1, const TcParams p,
+                        const TcParams p1) {
+  tc_gemm_body<3, AK, BKM, true, AK1, BK1>(&tmAh, &tmAl, &tmBh, &tmBl, &tmAh1, &tmAl1, &tmBh1,
+                                           &tmBl1, p, p1);
 }
 
 // ----------------------------------------------------------------- prepass
@@ -1046,10 +1135,16 @@ SplitPlan plan_split(int M, int N, int K, int num_sms, int passes) {
     helper_load = j * (num_kb - kp);
   }
   if (kp < 1 || kp >= num_kb || (s > 0 && len < 1)) return sp;
-  // worth it only if the last wave gets clearly shorter (partial tiles cost
-  // a write and a read of 128 KB each)
+  // Worth it only if the last wave gets shorter by more than the split
+  // costs: every part writes a 128 KB partial tile and the finishing CTA
+  // reads them back before its epilogue, some tens of microseconds that no
+  // other work hides (measured on B200: a 128-tile GEMM with K = 1000 split
+  // over 148 SMs ran 4x slower than whole tiles on 128).  So the last wave
+  // must lose at least 64 k-blocks, and a helper's tails must be long enough
+  // (32 k-blocks) for its partial-tile stores to hide behind its next tail.
   const int last = std::max(kp, helper_load);
-  if (last > num_kb * 9 / 10) return sp;
+  if (num_kb - last < 64) return sp;
+  if (j > 0 && num_kb - kp < 32) return sp;
   sp.mode = 2;
   sp.tile0 = tiles - r;
   sp.r = r;
@@ -1062,13 +1157,19 @@ SplitPlan plan_split(int M, int N, int K, int num_sms, int passes) {
   return sp;
 }
 
-int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
-                  const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s) {
-  if (M == 0 || N == 0) return kOk;
+namespace {
+// Tensor maps (A hi, A lo, B hi, B lo) and kernel parameters of one GEMM,
+// with its column-sum counters zeroed on stream s.  kOk, or an error code.
+int tc_prepare(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
+               const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s,
+               CUtensorMap (&maps)[4], TcParams& p) {
   if (K <= 0 || (passes != 1 && passes != 3)) return kErrInvalid;
   if (!A.hi || !B.hi || (passes == 3 && (!A.lo || !B.lo))) return kErrInvalid;
   if (!E.c && !E.c_hi) return kErrInvalid;
-  CUtensorMap tah{}, tal{}, tbh{}, tbl{};
+  CUtensorMap& tah = maps[0];
+  CUtensorMap& tal = maps[1];
+  CUtensorMap& tbh = maps[2];
+  CUtensorMap& tbl = maps[3];
   // plain TF32 runs 32-deep stages (stage_bk)
   const int bk = passes == 1 ? 32 : kBK;
   bool ok = operand_map(&tah, A.hi, A.kmajor, M, K, A.ld, kBM, A.padded, bk) &&
@@ -1081,7 +1182,7 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
     tbl = tbh;
   }
   if (!ok) return kErrUnsupported;
-  TcParams p{};
+  p = TcParams{};
   p.c = E.c; p.bias = E.bias; p.mask = E.mask; p.c_hi = E.c_hi; p.c_lo = E.c_lo;
   p.status = L.status; p.ldc = E.ldc; p.ldm = E.ldm;
   p.M = M; p.N = N; p.K = K;
@@ -1102,6 +1203,18 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
     cudaError_t me = cudaMemsetAsync(p.colsum_cnt, 0, sizeof(int) * p.tiles_n, s);
     if (me != cudaSuccess) return cuda_status(me);
   }
+  return kOk;
+}
+}  // namespace
+
+int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
+                  const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s) {
+  if (M == 0 || N == 0) return kOk;
+  CUtensorMap maps[4] = {};
+  TcParams p{};
+  const int rc = tc_prepare(L, A, B, E, M, N, K, passes, s, maps, p);
+  if (rc != kOk) return rc;
+  const CUtensorMap &tah = maps[0], &tal = maps[1], &tbh = maps[2], &tbl = maps[3];
   // Fewest CTAs that still finish the tiles in the same number of waves: a
   // 128- or 512-tile GEMM takes 128 SMs, leaving the rest to a concurrent
   // NCCL all-reduce at no cost to the GEMM (B200 has 148 SMs).
@@ -1139,10 +1252,126 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   return e == cudaSuccess ? kOk : cuda_status(e);
 }
 
+namespace {
+template <bool AK, bool BKM, bool AK1, bool BK1>
+cudaError_t launch_pair(const CUtensorMap (&m0)[4], const CUtensorMap (&m1)[4],
+                        const TcParams& p0, const TcParams& p1, int grid, cudaStream_t s) {
+  auto kern = tc_gemm_pair_kernel<AK, BKM, AK1, BK1>;
+  constexpr int kSmem = Cfg<3, kBK>::kSmem;
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(kern, kSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, kSmem, s>>>(m0[0], m0[1], m0[2], m0[3], m1[0], m1[1], m1[2], m1[3], p0,
+                                     p1);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+// Cost model of the pair decision, in k-blocks of one CTA (3xTF32 stages):
+// a launch costs its prologue, pipeline fill and last unhidden epilogue
+// (kLaunchKb); a split tile costs the partial-tile round trip (kFinishKb).
+constexpr int64_t kLaunchKb = 48, kFinishKb = 32;
+
+int64_t tiles_of(int M, int N) {
+  return static_cast<int64_t>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+}
+
+// Busiest CTA of one launch of its own, as tc_gemm_split schedules it.
+int64_t single_makespan(const TcPairGemm& g, int num_sms) {
+  const int64_t tiles = tiles_of(g.M, g.N), kb = (g.K + kBK - 1) / kBK;
+  const SplitPlan sp = plan_split(g.M, g.N, g.K, num_sms, 3);
+  const int64_t full = tiles / num_sms;
+  if (sp.mode == 2) {
+    const int64_t helper = sp.s > 0 ? kb - sp.kp - static_cast<int64_t>(sp.s - 1) * sp.len
+                                    : static_cast<int64_t>(sp.j) * (kb - sp.kp);
+    return full * kb + std::max<int64_t>(sp.kp, helper) + kFinishKb + kLaunchKb;
+  }
+  if (sp.mode == 1)
+    return full * kb + ((tiles - full * num_sms) * kb + num_sms - 1) / num_sms + kFinishKb +
+           kLaunchKb;
+  return (tiles + num_sms - 1) / num_sms * kb + kLaunchKb;
+}
+
+// Busiest CTA of the paired launch: a's tiles, then b's, round robin.
+int64_t pair_makespan(const TcPairGemm& a, const TcPairGemm& b, int num_sms) {
+  const int64_t ta = tiles_of(a.M, a.N), tb = tiles_of(b.M, b.N);
+  const int64_t ka = (a.K + kBK - 1) / kBK, kbb = (b.K + kBK - 1) / kBK;
+  const int64_t G = std::min<int64_t>(num_sms, ta + tb);
+  int64_t worst = 0;
+  for (int64_t c = 0; c < G; ++c) {
+    const int64_t na = c < ta ? (ta - c + G - 1) / G : 0;
+    // b's tile u sits at index ta + u; CTA c takes those with (ta + u) % G == c
+    const int64_t first = ((c - ta) % G + G) % G;
+    const int64_t nb = first < tb ? (tb - first + G - 1) / G : 0;
+    worst = std::max(worst, na * ka + nb * kbb);
+  }
+  return worst + kLaunchKb;
+}
+
+bool pair_pays(const TcPairGemm& a, const TcPairGemm& b, int num_sms) {
+  static const bool forced = [] {  // MX_PAIR=0: always two launches
+    const char* e = std::getenv("MX_PAIR");
+    return e && e[0] == '0';
+  }();
+  if (forced) return false;
+  return pair_makespan(a, b, num_sms) <= single_makespan(a, num_sms) + single_makespan(b, num_sms);
+}
+}  // namespace
+
+int tc_gemm_pair(const TcLaunch& L, const TcPairGemm& g0, const TcPairGemm& g1, cudaStream_t s) {
+  if (g0.M == 0 || g0.N == 0) return tc_gemm_split(L, g1.A, g1.B, g1.E, g1.M, g1.N, g1.K, 3, s);
+  if (g1.M == 0 || g1.N == 0) return tc_gemm_split(L, g0.A, g0.B, g0.E, g0.M, g0.N, g0.K, 3, s);
+  // the GEMM with the longer tiles (more k-blocks) first: every CTA starts
+  // on one of them and the short tiles fill in behind
+  const bool swap = g1.K > g0.K;
+  const TcPairGemm& a = swap ? g1 : g0;
+  const TcPairGemm& b = swap ? g0 : g1;
+  const int la = (a.A.kmajor ? 2 : 0) | (a.B.kmajor ? 1 : 0);
+  const int lb = (b.A.kmajor ? 2 : 0) | (b.B.kmajor ? 1 : 0);
+  // the layout pairs of a Linear layer's backward (dX: A k-major; dW: both
+  // MN-major); others run as two launches
+  using Fn = cudaError_t (*)(const CUtensorMap (&)[4], const CUtensorMap (&)[4], const TcParams&,
+                             const TcParams&, int, cudaStream_t);
+  Fn fn = nullptr;
+  if (la == 3 && lb == 0) fn = launch_pair<true, true, false, false>;
+  else if (la == 0 && lb == 3) fn = launch_pair<false, false, true, true>;
+  else if (la == 2 && lb == 0) fn = launch_pair<true, false, false, false>;
+  else if (la == 0 && lb == 2) fn = launch_pair<false, false, true, false>;
+  if (!fn) {
+    const int rc = tc_gemm_split(L, g0.A, g0.B, g0.E, g0.M, g0.N, g0.K, 3, s);
+    return rc != kOk ? rc : tc_gemm_split(L, g1.A, g1.B, g1.E, g1.M, g1.N, g1.K, 3, s);
+  }
+  if (!pair_pays(a, b, L.num_sms)) {
+    const int rc = tc_gemm_split(L, g0.A, g0.B, g0.E, g0.M, g0.N, g0.K, 3, s);
+    return rc != kOk ? rc : tc_gemm_split(L, g1.A, g1.B, g1.E, g1.M, g1.N, g1.K, 3, s);
+  }
+  CUtensorMap ma[4] = {}, mb[4] = {};
+  TcParams pa{}, pb{};
+  int rc = tc_prepare(L, a.A, a.B, a.E, a.M, a.N, a.K, 3, s, ma, pa);
+  if (rc != kOk) return rc;
+  rc = tc_prepare(L, b.A, b.B, b.E, b.M, b.N, b.K, 3, s, mb, pb);
+  if (rc != kOk) return rc;
+  pa.pair_tiles = pb.num_tiles;
+  const int total = pa.num_tiles + pb.num_tiles;
+  const int grid = std::min(L.num_sms, total);
+  const cudaError_t e = fn(ma, mb, pa, pb, grid, s);
+  return e == cudaSuccess ? kOk : cuda_status(e);
+}
+
 size_t tc_colsum_scratch_bytes(int M, int N) {
   if (M <= 0 || N <= 0) return 0;
   const size_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
   return align256(sizeof(float) * tiles_m * N) + align256(sizeof(int) * tiles_n);
+}
+
+void tc_split_plan(int M, int N, int K, int num_sms, int passes, int32_t* out) {
+  const SplitPlan sp = plan_split(M, N, K, num_sms, passes);
+  out[0] = sp.mode;
+  out[1] = sp.tile0;
+  out[2] = sp.r;
+  out[3] = sp.kp;
+  out[4] = sp.s;
+  out[5] = sp.j;
 }
 
 size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes) {

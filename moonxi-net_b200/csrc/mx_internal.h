@@ -141,6 +141,21 @@ struct TcEpilogue {
 size_t tc_colsum_scratch_bytes(int M, int N);
 int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
                   const TcEpilogue& E, int M, int N, int K, int passes, cudaStream_t s);
+// One GEMM of a paired launch (3xTF32 split operands).
+struct TcPairGemm {
+  SplitOperand A, B;
+  TcEpilogue E;
+  int M = 0, N = 0, K = 0;
+};
+// Two independent 3xTF32 GEMMs in one persistent launch (whole tiles, the
+// GEMM with more k-blocks per tile first); layout pairs other than those of
+// a Linear layer's backward (dX with a K-major A, dW with both operands
+// MN-major) run as two launches.
+int tc_gemm_pair(const TcLaunch& L, const TcPairGemm& g0, const TcPairGemm& g1, cudaStream_t s);
+// The split plan tc_gemm_split picks for a shape: out[0..5] = mode (0 whole
+// tiles, 1 stream-K, 2 tail split), first split tile, remainder tiles r,
+// primary k-blocks kp, pieces per tail s, tails per helper j.
+void tc_split_plan(int M, int N, int K, int num_sms, int passes, int32_t* out);
 // hi/lo split of a row-major [rows][cols] matrix (leading dimension ld) into
 // hi/lo with leading dimension ld_out.
 int split_tf32(Context* ctx, const float* src, int64_t ld, int rows, int cols, float* hi,

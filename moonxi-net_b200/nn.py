@@ -156,7 +156,8 @@ class MLP:
     def __init__(self, dims, weights=None, biases=None, layout: str = "nn", device=None,
                  precision="default", lr: float = 0.01, momentum: float = 0.9,
                  weight_decay: float = 1e-4, max_grad_norm: float = 35.0,
-                 process_group=None, fused=None, shard_update=None, collectives=None):
+                 process_group=None, fused=None, shard_update=None, collectives=None,
+                 pair_backward=None):
         if layout not in ("nn", "nt"):
             raise ValueError("layout must be 'nn' (w [in,out]) or 'nt' (w [out,in])")
         self.dims = list(dims)
@@ -264,6 +265,8 @@ class MLP:
         # the exposed tail (the chunked GEMMs lose more than the overlap
         # gains), so one chunk is the default
         self.last_bucket_chunks = 1
+        # each hidden layer's backward GEMMs (dX and dW) as one paired launch
+        self.pair_backward = pair_backward is not False
 
     # ------------------------------------------------------------------ state
     def _wshape(self, i):
@@ -442,6 +445,17 @@ class MLP:
             e1.record()
             timer.append((flops, e0, e1))
 
+        def gemm_pair(flops, k0, k1):
+            k0, k1 = dict(k0, padded=3), dict(k1, padded=3)
+            if timer is None:
+                return ops.gemm_split_pair(k0, k1, ctx=ctx)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ops.gemm_split_pair(k0, k1, ctx=ctx)
+            e1.record()
+            timer.append((flops, e0, e1))
+
         marks = self.phase_marks
 
         def mark(name):
@@ -499,34 +513,46 @@ class MLP:
             rows_per = -(-Mrows // nchunk)
             rows_per = -(-rows_per // 128) * 128
             bstart, bend = self.layout_.bucket(i)
+            dws = []  # (flops, kwargs, [lo, hi) of the gradient buffer) per row chunk
             r0 = 0
             while r0 < Mrows:
                 r1 = min(Mrows, r0 + rows_per)
                 if nt:   # dW[out,in] = dY^T X
-                    gemm(2 * B * (r1 - r0) * Ncols, a_hi=gh.view(-1)[r0:], a_lo=gl.view(-1)[r0:],
-                         lda=fo, a_kmajor=False, b_hi=hh, b_lo=hl, ldb=fi, b_kmajor=False,
-                         M=r1 - r0, K=B, N=fi, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
+                    kw = dict(a_hi=gh.view(-1)[r0:], a_lo=gl.view(-1)[r0:], lda=fo,
+                              a_kmajor=False, b_hi=hh, b_lo=hl, ldb=fi, b_kmajor=False,
+                              M=r1 - r0, K=B, N=fi, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
                 else:    # dW[in,out] = X^T dY
-                    gemm(2 * B * (r1 - r0) * Ncols, a_hi=hh.view(-1)[r0:], a_lo=hl.view(-1)[r0:],
-                         lda=fi, a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo, b_kmajor=False,
-                         M=r1 - r0, K=B, N=fo, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
-                if self.coll is not None and nchunk > 1:
-                    lo = bstart if r0 == 0 else _LOSS_SLOTS + self.w_off[i] + r0 * Ncols
-                    hi = bend if r1 == Mrows else _LOSS_SLOTS + self.w_off[i] + r1 * Ncols
-                    works.append(self.coll.all_reduce(self.grads_buf[lo:hi]))
+                    kw = dict(a_hi=hh.view(-1)[r0:], a_lo=hl.view(-1)[r0:], lda=fi,
+                              a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo, b_kmajor=False,
+                              M=r1 - r0, K=B, N=fo, c=self.gw[i].view(-1)[r0 * Ncols:], ldc=Ncols)
+                lo = bstart if r0 == 0 else _LOSS_SLOTS + self.w_off[i] + r0 * Ncols
+                hi = bend if r1 == Mrows else _LOSS_SLOTS + self.w_off[i] + r1 * Ncols
+                dws.append((2 * B * (r1 - r0) * Ncols, kw, lo, hi))
                 r0 = r1
+            dx = None
+            if i > 0:
+                # dX = (dY W^T) masked by relu'(h_i); split copy for the next GEMMs
+                ph, pl = gsplit[i - 1]
+                dx = (2 * B * fi * fo,
+                      dict(a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True, b_hi=self.w_hi[i],
+                           b_lo=self.w_lo[i], ldb=fi if nt else fo, b_kmajor=not nt, M=B, K=fo,
+                           N=fi, c=gbuf[i - 1], c_hi=ph, c_lo=pl, mask=acts[i - 1], ldm=fi,
+                           colsum=self.gb[i - 1], colsum_scratch=cs_scratch))
+            if dx is not None and len(dws) == 1 and self.pair_backward:
+                # dX and dW read the same dY and not each other: one launch
+                gemm_pair(dx[0] + dws[0][0], dx[1], dws[0][1])
+                dx = None
+            else:
+                for fl, kw, lo, hi in dws:
+                    gemm(fl, **kw)
+                    if self.coll is not None and nchunk > 1:
+                        works.append(self.coll.all_reduce(self.grads_buf[lo:hi]))
             if plan is not None:
                 works.append(plan.reduce_scatter(self.grads_buf, i, self.coll))
             elif self.coll is not None and nchunk == 1:
                 works.append(self.coll.all_reduce(self.bucket(i)))
-            if i > 0:
-                # dX = (dY W^T) masked by relu'(h_i); split copy for the next GEMMs
-                ph, pl = gsplit[i - 1]
-                gemm(2 * B * fi * fo, a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True,
-                     b_hi=self.w_hi[i], b_lo=self.w_lo[i], ldb=fi if nt else fo,
-                     b_kmajor=not nt, M=B, K=fo, N=fi, c=gbuf[i - 1], c_hi=ph, c_lo=pl,
-                     mask=acts[i - 1], ldm=fi, colsum=self.gb[i - 1],
-                     colsum_scratch=cs_scratch)
+            if dx is not None:
+                gemm(dx[0], **dx[1])
         mark("backward")
         for wk in works:
             wk.wait()

@@ -269,6 +269,43 @@ def gemm_colsum_scratch_bytes(M: int, N: int) -> int:
     return int(_lib.lib().mx_gemm_colsum_scratch_bytes(M, N))
 
 
+def _split_gemm(a_hi, a_lo, lda: int, a_kmajor: bool, b_hi, b_lo, ldb: int, b_kmajor: bool,
+                M: int, K: int, N: int, c=None, c_hi=None, c_lo=None, ldc: int | None = None,
+                alpha: float = 1.0, beta: float = 0.0, bias=None, relu: bool = False,
+                mask=None, ldm: int = 0, padded: int = 0, colsum=None, colsum_scratch=None):
+    g = _lib.SplitGemm()
+    g.a_hi, g.a_lo, g.lda, g.a_kmajor = a_hi.data_ptr(), _ptr(a_lo), lda, int(a_kmajor)
+    g.b_hi, g.b_lo, g.ldb, g.b_kmajor = b_hi.data_ptr(), _ptr(b_lo), ldb, int(b_kmajor)
+    g.c, g.c_hi, g.c_lo = _ptr(c), _ptr(c_hi), _ptr(c_lo)
+    g.ldc = N if ldc is None else ldc
+    g.M, g.K, g.N, g.alpha, g.beta = M, K, N, float(alpha), float(beta)
+    g.bias, g.relu, g.mask, g.ldm, g.flags = _ptr(bias), int(relu), _ptr(mask), ldm, int(padded)
+    if colsum is not None:
+        g.colsum, g.colsum_scratch = colsum.data_ptr(), colsum_scratch.data_ptr()
+        g.colsum_scratch_bytes = colsum_scratch.numel() * colsum_scratch.element_size()
+    return g
+
+
+def gemm_split_pair(g0: dict, g1: dict, ctx=None, stream=None) -> None:
+    """Two independent 3xTF32 split-operand GEMMs in one launch
+    (mx_gemm_split_pair): each dict holds gemm_split's keyword arguments
+    (a_hi ... colsum_scratch; passes is always 3)."""
+    s0, s1 = _split_gemm(**g0), _split_gemm(**g1)
+    rc = _lib.lib().mx_gemm_split_pair(_handle(ctx, g0["a_hi"]), ctypes.byref(s0),
+                                       ctypes.byref(s1), _stream_ptr(stream))
+    check(rc, "mx_gemm_split_pair")
+
+
+def split_plan(M: int, N: int, K: int, passes: int = 3, ctx=None, device: int | None = None):
+    """The work split the context's tcgen05 GEMM picks for M x N x K
+    (mx_tc_split_plan): dict of mode (0 whole tiles, 1 stream-K, 2 tail
+    split), tile0, r, kp, s, j."""
+    out = (ctypes.c_int32 * 6)()
+    h = ctx if ctx is not None else context(device)
+    check(_lib.lib().mx_tc_split_plan(h, M, N, K, passes, out), "mx_tc_split_plan")
+    return dict(zip(("mode", "tile0", "r", "kp", "s", "j"), (int(v) for v in out)))
+
+
 def softmax_ce_colsum_scratch_bytes(batch: int, C: int) -> int:
     """0 when C is too large for the fused column sums."""
     return int(_lib.lib().mx_softmax_ce_colsum_scratch_bytes(batch, C))

@@ -72,6 +72,11 @@ def test_calls_without_device_report_status():
     assert L.moonbit_cuda_matmul(None, p, p, p, 2, 2, 2, 0, 0, 1.0, 0.0) == _lib.MX_ERR_NO_DEVICE
     assert L.mx_context_create(0) is None
     assert L.mx_relu_backward(None, p, p, p, 4, None) == _lib.MX_ERR_NO_DEVICE
+    g = _lib.SplitGemm()
+    assert L.mx_gemm_split_pair(None, ctypes.byref(g), ctypes.byref(g), None) == \
+        _lib.MX_ERR_NO_DEVICE
+    out = (ctypes.c_int32 * 6)()
+    assert L.mx_tc_split_plan(None, 128, 256, 64, 3, out) == _lib.MX_ERR_NO_DEVICE
 
 
 def test_product_does_not_import_oracle():

@@ -174,16 +174,21 @@ def test_split_step_matches_per_call_3xtf32(cuda_device, layout):
     assert rel <= 1e-6
 
 
-@pytest.mark.parametrize("M,K,N,a_k,b_k", [
-    (1024, 4096, 4096, True, True),    # 128 tiles on 148 SMs: whole tails, 7 per helper
-    (4096, 1024, 4096, False, False),  # 3 full waves + 68 tiles: one piece per helper
-    (1152, 2048, 2304, True, False),   # 81 tiles on 148 SMs: whole tails, 2 per helper
+@pytest.mark.parametrize("M,K,N,a_k,b_k,branch", [
+    (1024, 16384, 4096, True, True, "tails"),    # 128 tiles on 148 SMs: 7 tails per helper
+    (4096, 2048, 4096, False, False, "pieces"),  # 3 full waves + 68 tiles: one piece each
+    (1152, 8192, 2304, True, False, "tails"),    # 81 tiles on 148 SMs: 2 tails per helper
 ])
-def test_tail_split_waves(cuda_device, M, K, N, a_k, b_k):
-    """Shapes whose last wave of tiles is part-filled run the tail split (the
-    remainder tiles' first k-blocks on their own CTAs, the rest on the idle
-    ones, parts summed in k order by the last to finish): fp32-class against
-    fp64, bit-identical run to run, with the fused column sums and mask."""
+def test_tail_split_waves(cuda_device, M, K, N, a_k, b_k, branch):
+    """Shapes whose last wave of tiles is part-filled, with K deep enough
+    for the split to pay, run the tail split (the remainder tiles' first
+    k-blocks on their own CTAs, the rest on the idle ones, parts summed in k
+    order by the last to finish): fp32-class against fp64, bit-identical run
+    to run, with the fused column sums and mask."""
+    plan = ops.split_plan(M, N, K)
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    assert plan["mode"] == 2 and (plan["s"] > 0) == (branch == "pieces"), plan
     g = torch.Generator("cuda").manual_seed(M + N)
     A = torch.randn(M, K, device="cuda", generator=g)
     B = torch.randn(K, N, device="cuda", generator=g)
@@ -208,3 +213,86 @@ def test_tail_split_waves(cuda_device, M, K, N, a_k, b_k):
     want = c.double().sum(0)
     assert float(((cs.double() - want).abs() / c.double().abs().sum(0)).max()) <= \
         1e-6 * math.sqrt(M)
+
+
+def test_split_plan_skips_unprofitable_tails(cuda_device):
+    """A part-filled last wave whose split would save fewer k-blocks than
+    the partial tiles cost runs whole tiles: the 1024-row layers of the
+    wide MLP (128 tiles of K = 4096 or 1000 on 148 SMs)."""
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    for M, N, K in ((1024, 4096, 4096), (1024, 4096, 1000), (4096, 1000, 1024),
+                    (4096, 4096, 1024)):
+        assert ops.split_plan(M, N, K)["mode"] == 0, (M, N, K)
+
+
+def _layer_backward(B, fi, fo, nt, seed):
+    """Operands of one Linear layer's backward in split form, as the MLP step
+    holds them: dY [B, fo], activation h [B, fi] (ReLU mask), weights
+    (nn: [fi, fo], nt: [fo, fi]); the keyword arguments of the dX and dW
+    GEMMs and their fp64 references."""
+    g = torch.Generator("cuda").manual_seed(seed)
+    dY = torch.randn(B, fo, device="cuda", generator=g)
+    h = torch.randn(B, fi, device="cuda", generator=g)
+    W = torch.randn(fo, fi, device="cuda", generator=g) if nt else \
+        torch.randn(fi, fo, device="cuda", generator=g)
+    gh, gl = _split(dY)
+    hh, hl = _split(h)
+    wh, wl = _split(W)
+    out = dict(dx=torch.empty(B, fi, device="cuda"), dx_hi=torch.empty(B, fi, device="cuda"),
+               dx_lo=torch.empty(B, fi, device="cuda"), cs=torch.empty(fi, device="cuda"),
+               dw=torch.empty(*((fo, fi) if nt else (fi, fo)), device="cuda"),
+               scratch=torch.empty(ops.gemm_colsum_scratch_bytes(B, fi) // 4, device="cuda"))
+    dx_kw = dict(a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True, b_hi=wh, b_lo=wl,
+                 ldb=fi if nt else fo, b_kmajor=not nt, M=B, K=fo, N=fi, c=out["dx"],
+                 c_hi=out["dx_hi"], c_lo=out["dx_lo"], mask=h, ldm=fi, colsum=out["cs"],
+                 colsum_scratch=out["scratch"], padded=3)
+    if nt:   # dW[out, in] = dY^T h
+        dw_kw = dict(a_hi=gh, a_lo=gl, lda=fo, a_kmajor=False, b_hi=hh, b_lo=hl, ldb=fi,
+                     b_kmajor=False, M=fo, K=B, N=fi, c=out["dw"], padded=3)
+    else:    # dW[in, out] = h^T dY
+        dw_kw = dict(a_hi=hh, a_lo=hl, lda=fi, a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo,
+                     b_kmajor=False, M=fi, K=B, N=fo, c=out["dw"], padded=3)
+    Wt = W.double() if nt else W.double().t()           # [fo, fi]
+    dx_ref = (dY.double() @ Wt) * (h > 0)
+    dx_scale = (dY.double().abs() @ Wt.abs())
+    dw_ref = dY.double().t() @ h.double() if nt else h.double().t() @ dY.double()
+    dw_scale = dY.double().abs().t() @ h.double().abs() if nt else \
+        h.double().abs().t() @ dY.double().abs()
+    return dx_kw, dw_kw, out, (dx_ref, dx_scale, dw_ref, dw_scale)
+
+
+@pytest.mark.parametrize("B,fi,fo,nt", [
+    (1024, 4096, 4096, False),   # the wide MLP's hidden layer at 8 GPUs (1024 rows each)
+    (1024, 4096, 1000, False),   # ... and its output layer
+    (8192, 1024, 512, False),    # dW with the longer tiles: it goes first
+    (200, 300, 132, False),      # ragged: partial tiles in every dimension
+    (200, 300, 132, True),
+    (512, 1024, 1024, True),
+])
+def test_gemm_split_pair_matches_two_launches(cuda_device, B, fi, fo, nt):
+    """mx_gemm_split_pair (a layer's dX and dW in one launch) against the
+    same two GEMMs launched one by one: bit-identical when the single
+    launches also run whole tiles, and fp32-class against fp64 always --
+    the masked dX with its split copies and column sums, and dW."""
+    dx_kw, dw_kw, out, (dx_ref, dx_scale, dw_ref, dw_scale) = _layer_backward(B, fi, fo, nt, B + fi)
+    ops.gemm_split_pair(dx_kw, dw_kw)
+    paired = {k: v.clone() for k, v in out.items() if k != "scratch"}
+    ops.gemm_split(**dx_kw)
+    ops.gemm_split(**dw_kw)
+    torch.cuda.synchronize()
+    assert ops.context_status(ops.context(0))[0] == 0
+    whole = ops.split_plan(B, fi, fo)["mode"] == 0 and \
+        ops.split_plan(dw_kw["M"], dw_kw["N"], B)["mode"] == 0
+    if whole:
+        for k, v in paired.items():
+            assert torch.equal(v, out[k]), k
+    tol = 1e-5
+    assert float(((paired["dx"].double() - dx_ref).abs() / dx_scale.clamp_min(1e-30)).max()) \
+        <= tol * math.sqrt(fo)
+    assert float(((paired["dw"].double() - dw_ref).abs() / dw_scale).max()) <= tol * math.sqrt(B)
+    assert torch.equal(paired["dx_hi"], _rna_tf32(paired["dx"]))
+    assert torch.equal(paired["dx_lo"], _rna_tf32(paired["dx"] - paired["dx_hi"]))
+    want = paired["dx"].double().sum(0)
+    assert float(((paired["cs"].double() - want).abs() /
+                  paired["dx"].double().abs().sum(0).clamp_min(1e-30)).max()) <= 1e-6 * math.sqrt(B)

@@ -111,24 +111,6 @@ struct TcParams {
   int pair_tiles;
 };
 
-// Column sums of a warp's 32 x 32 block (lane = row, x[j] = column j):
-// afterwards x[0] of lane l holds the sum over the 32 rows of column l.
-// Butterfly reduce-scatter: at each step a lane keeps the half of its
-// columns selected by its lane bit and adds the partner's copy of that half
-// (31 shuffles for 32 columns).  Fixed order: deterministic.
-__device__ __forceinline__ void warp_colsum32(float (&x)[32], int lane) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < o; ++i) {
-      const float send = upper ? x[i] : x[i + o];
-      const float keep = upper ? x[i + o] : x[i];
-      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-  }
-}
-
 // Grouped raster: bands of 16 M-tiles, N-major inside a band, so the CTAs
 // running at one time share A and B tiles in L2.
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -314,86 +296,46 @@ __device__ __forceinline__ int64_t part_slot(const TcParams& p, int t, int num_k
   return r + static_cast<int64_t>(i % H) * p.tail_j + i / H;            // the helper's tail
 }
 
-// Epilogue of one 32-column chunk of one output row: v holds alpha-less
-// accumulator values; applies alpha/beta/bias/ReLU/mask, stores c and the
-// hi/lo split.
-__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0,
-                                            float (&acc)[32], bool vec_ok, bool mask_vec) {
-  const int64_t roff = static_cast<int64_t>(row) * p.ldc;
-  const bool full_chunk = col0 + 32 <= p.N;
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float x = p.alpha * acc[j];
-    const int col = col0 + j;
-    if (col < p.N) {
-      if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col];
-      if (p.bias) x = x + __ldg(p.bias + col);
-      if (p.relu) x = x > 0.0f ? x : 0.0f;
-    }
-    v[j] = x;
-  }
+// Epilogue of one column of 32 consecutive rows (row0.., col), the lane =
+// column layout after the warp's transpose: a warp's loads and stores at one
+// row are 32 consecutive floats.  v holds alpha-less accumulator values;
+// applies alpha/beta/bias/ReLU/mask, stores c and the hi/lo split, and leaves
+// the stored values in v (zero where nothing is stored).
+__device__ __forceinline__ void store_rows(const TcParams& p, int row0, int col, float (&v)[32]) {
+  const bool colok = col < p.N;
+  const float b = (p.bias && colok) ? __ldg(p.bias + col) : 0.0f;
+  float m[32];
   if (p.mask) {
-    const float* mrow = p.mask + static_cast<int64_t>(row) * p.ldm + col0;
-    if (mask_vec && full_chunk) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 m4 = __ldg(reinterpret_cast<const float4*>(mrow + j));
-        v[j] = m4.x > 0.0f ? v[j] : 0.0f;
-        v[j + 1] = m4.y > 0.0f ? v[j + 1] : 0.0f;
-        v[j + 2] = m4.z > 0.0f ? v[j + 2] : 0.0f;
-        v[j + 3] = m4.w > 0.0f ? v[j + 3] : 0.0f;
+    for (int i = 0; i < 32; ++i)
+      m[i] = (colok && row0 + i < p.M)
+                 ? __ldg(p.mask + static_cast<int64_t>(row0 + i) * p.ldm + col) : 0.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int row = row0 + i;
+    float x = p.alpha * v[i];
+    if (colok && row < p.M) {
+      const int64_t off = static_cast<int64_t>(row) * p.ldc + col;
+      if (p.beta != 0.0f) x = x + p.beta * p.c[off];
+      if (p.bias) x = x + b;
+      if (p.relu) x = x > 0.0f ? x : 0.0f;
+      if (p.mask && !(m[i] > 0.0f)) x = 0.0f;
+      if (p.c) p.c[off] = x;
+      if (p.c_hi) {
+        const float h = __uint_as_float(f32_to_tf32_rna(x));
+        p.c_hi[off] = h;
+        if (p.c_lo) p.c_lo[off] = __uint_as_float(f32_to_tf32_rna(x - h));
       }
     } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < p.N) v[j] = __ldg(mrow + j) > 0.0f ? v[j] : 0.0f;
+      x = 0.0f;
     }
+    v[i] = x;
   }
-  if (p.c) {
-    float* crow = p.c + roff;
-    if (vec_ok && full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < p.N) crow[col0 + j] = v[j];
-    }
-  }
-  if (p.c_hi) {
-    float hv[32], lv[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t h = f32_to_tf32_rna(v[j]);
-      hv[j] = __uint_as_float(h);
-      lv[j] = __uint_as_float(f32_to_tf32_rna(v[j] - hv[j]));
-    }
-    float* hrow = p.c_hi + roff;
-    float* lrow = p.c_lo ? p.c_lo + roff : nullptr;
-    if (vec_ok && full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        *reinterpret_cast<float4*>(hrow + col0 + j) = make_float4(hv[j], hv[j + 1], hv[j + 2], hv[j + 3]);
-        if (lrow)
-          *reinterpret_cast<float4*>(lrow + col0 + j) = make_float4(lv[j], lv[j + 1], lv[j + 2], lv[j + 3]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < p.N) {
-          hrow[col0 + j] = hv[j];
-          if (lrow) lrow[col0 + j] = lv[j];
-        }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = v[j];  // the stored values, for column sums
 }
 
 // Epilogue of four consecutive outputs (row, col..col+3): the same math as
-// store_chunk for a 4-wide group.
+// store_rows for a 4-wide group.
 __device__ __forceinline__ float4 store_quad(const TcParams& p, int row, int col, float4 acc,
                                              bool vec_ok, bool mask_vec) {
   const int64_t roff = static_cast<int64_t>(row) * p.ldc;
@@ -706,6 +648,7 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
     __shared__ int sk_last;  // broadcast of the arrival test among the epilogue warps
     __shared__ int cs_last;
     __shared__ __align__(16) float cs_warp[4][kBN];  // column sums of parts of the tile's rows
+    __shared__ float tr_buf[4][32 * 33];              // per-warp transpose, padded: no conflicts
     // The tile's column sums into colsum_part[tm] (value(c) for the tile's
     // column c), then the arrival test of its N-tile column: the last M-tile
     // to arrive adds every M-tile's row in order (the result does not depend
@@ -762,40 +705,40 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
       const bool vec_ok = vec_of(q), mask_vec = mask_vec_of(q);
       int tm, tn;
       tile_coords(t, q.tiles_m, q.tiles_n, tm, tn);
-      const int row = tm * kBM + row_in_tile;
       const bool whole = q1 || (kb0 == 0 && kb1 == num_kb);
-      // partial tile: this CTA's slot
-      float* slot = nullptr;
-      if (!whole)
-        slot = p.sk_partials + own_slot(p, t, num_kb) * (kBM * kBN) +
-               static_cast<int64_t>(row_in_tile) * kBN;
+      const int rbase = lane_grp * 32;  // this warp's first row in the tile
+      float* tw = &tr_buf[lane_grp][0];
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         uint32_t r[32];
-        __syncwarp();
+        __syncwarp();  // the previous chunk's transpose reads are done
         tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * kBN +
                            chunk * 32,
                        r);
         tmem_wait_ld();
+        // Transpose the warp's 32 x 32 block (lane = row -> lane = column),
+        // so that every global load and store below is one 128-byte line.
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = __uint_as_float(r[j]);
+        __syncwarp();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = tw[i * 33 + lane];
         if (whole) {
-          const int col0 = tn * kBN + chunk * 32;
-          const bool live = row < q.M && col0 < q.N;
-          float a[32];
+          const int col = tn * kBN + chunk * 32 + lane;
+          store_rows(q, tm * kBM + rbase, col, v);
+          if (q.colsum) {  // rows past M and columns past N hold zero
+            float cs = 0.0f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) a[j] = __uint_as_float(r[j]);
-          if (live) store_chunk(q, row, col0, a, vec_ok, mask_vec);
-          if (q.colsum) {  // whole warp: rows past M and columns past N add zero
-#pragma unroll
-            for (int j = 0; j < 32; ++j) a[j] = (live && col0 + j < q.N) ? a[j] : 0.0f;
-            warp_colsum32(a, lane);
-            cs_warp[lane_grp][chunk * 32 + lane] = a[0];
+            for (int i = 0; i < 32; ++i) cs += v[i];
+            cs_warp[lane_grp][chunk * 32 + lane] = cs;
           }
         } else {
+          // partial tile: this CTA's slot, [row][256 columns]
+          float* slot = p.sk_partials + own_slot(p, t, num_kb) * (kBM * kBN) +
+                        static_cast<int64_t>(rbase) * kBN + chunk * 32 + lane;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(slot + chunk * 32 + j) =
-                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          for (int i = 0; i < 32; ++i) slot[static_cast<int64_t>(i) * kBN] = v[i];
         }
       }
       tc_fence_before();

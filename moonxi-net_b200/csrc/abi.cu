@@ -403,8 +403,9 @@ int gemm_split(void* handle, const float* a_hi, const float* a_lo, int64_t lda, 
   if (mask && ldm < N) return MX_ERR_INVALID;
   if (!c_hi && c_lo) return MX_ERR_INVALID;
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
+  L.all_sms = ctx->num_sms;
   L.sched = ctx->sched;
-  const size_t sk = tc_streamk_bytes(M, N, K, ctx->tc_sms(), passes);
+  const size_t sk = tc_split_scratch(ctx, M, N, K, passes);
   if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
     L.ws = ctx->workspace;
     L.ws_bytes = ctx->ws_bytes;
@@ -486,10 +487,11 @@ MX_EXPORT int32_t mx_gemm_split_pair(void* handle, const mx_split_gemm* g0,
   if (rc == kOk) rc = pair_gemm(g1, b);
   if (rc != kOk) return rc;
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
+  L.all_sms = ctx->num_sms;
   // a layout pair without a paired kernel runs as two launches, which may
   // split K and then need the stream-K scratch
-  const size_t sk = std::max(tc_streamk_bytes(a.M, a.N, a.K, ctx->tc_sms(), 3),
-                             tc_streamk_bytes(b.M, b.N, b.K, ctx->tc_sms(), 3));
+  const size_t sk = std::max(tc_split_scratch(ctx, a.M, a.N, a.K, 3),
+                             tc_split_scratch(ctx, b.M, b.N, b.K, 3));
   if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
     L.ws = ctx->workspace;
     L.ws_bytes = ctx->ws_bytes;
@@ -504,7 +506,8 @@ MX_EXPORT int32_t mx_tc_split_plan(void* handle, int32_t M, int32_t N, int32_t K
   Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   if (!out || M < 1 || N < 1 || K < 1 || (passes != 1 && passes != 3)) return MX_ERR_INVALID;
-  tc_split_plan(M, N, K, ctx->tc_sms(), passes, out);
+  tc_split_plan(M, N, K, tc_launch_sms(M, N, K, ctx->tc_sms(), ctx->num_sms, passes),
+                passes, out);
   return MX_OK;
 }
 
@@ -596,9 +599,9 @@ MX_EXPORT uint64_t mx_matmul_workspace_bytes(void* handle, int32_t M, int32_t K,
   GemmArgs g = ref_args(nullptr, nullptr, nullptr, M, K, N, transpose_a, transpose_b, 1.0f, 0.0f);
   const int p = resolve_precision(c, M, K, N, precision);
   if (p == MX_PREC_3XTF32)
-    return tc_gemm_workspace_bytes(g, 3) + tc_streamk_bytes(M, N, K, c->tc_sms(), 3);
+    return tc_gemm_workspace_bytes(g, 3) + tc_split_scratch(c, M, N, K, 3);
   if (p == MX_PREC_TF32)
-    return tc_gemm_workspace_bytes(g, 1) + tc_streamk_bytes(M, N, K, c->tc_sms(), 1);
+    return tc_gemm_workspace_bytes(g, 1) + tc_split_scratch(c, M, N, K, 1);
   if (p == MX_PREC_NPARRAY) return 0;  // no split-K in NpArray order
   return simt_gemm_scratch_bytes(c, g);
 }

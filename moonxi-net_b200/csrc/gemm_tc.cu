@@ -1101,6 +1101,60 @@ SplitPlan plan_split(int M, int N, int K, int num_sms, int passes) {
 }
 
 namespace {
+// Cost model of the launch decisions, in k-blocks of one CTA: a launch
+// costs its prologue, pipeline fill and last unhidden epilogue (kLaunchKb); a
+// split tile costs the partial-tile round trip (kFinishKb).
+constexpr int64_t kLaunchKb = 48, kFinishKb = 32;
+
+int64_t tiles_of(int M, int N) {
+  return static_cast<int64_t>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+}
+
+// Busiest CTA of one launch of its own on num_sms SMs, as tc_gemm_split
+// schedules it.
+int64_t gemm_makespan(int M, int N, int K, int num_sms, int passes) {
+  const int bk = passes == 1 ? 32 : kBK;
+  const int64_t tiles = tiles_of(M, N), kb = (K + bk - 1) / bk;
+  const SplitPlan sp = plan_split(M, N, K, num_sms, passes);
+  const int64_t full = tiles / num_sms;
+  if (sp.mode == 2) {
+    const int64_t helper = sp.s > 0 ? kb - sp.kp - static_cast<int64_t>(sp.s - 1) * sp.len
+                                    : static_cast<int64_t>(sp.j) * (kb - sp.kp);
+    return full * kb + std::max<int64_t>(sp.kp, helper) + kFinishKb + kLaunchKb;
+  }
+  if (sp.mode == 1)
+    return full * kb + ((tiles - full * num_sms) * kb + num_sms - 1) / num_sms + kFinishKb +
+           kLaunchKb;
+  return (tiles + num_sms - 1) / num_sms * kb + kLaunchKb;
+}
+
+// Busiest CTA of the paired launch: a's tiles, then b's, round robin.
+int64_t pair_makespan(const TcPairGemm& a, const TcPairGemm& b, int num_sms) {
+  const int64_t ta = tiles_of(a.M, a.N), tb = tiles_of(b.M, b.N);
+  const int64_t ka = (a.K + kBK - 1) / kBK, kbb = (b.K + kBK - 1) / kBK;
+  const int64_t G = std::min<int64_t>(num_sms, ta + tb);
+  int64_t worst = 0;
+  for (int64_t c = 0; c < G; ++c) {
+    const int64_t na = c < ta ? (ta - c + G - 1) / G : 0;
+    // b's tile u sits at index ta + u; CTA c takes those with (ta + u) % G == c
+    const int64_t first = ((c - ta) % G + G) % G;
+    const int64_t nb = first < tb ? (tb - first + G - 1) / G : 0;
+    worst = std::max(worst, na * ka + nb * kbb);
+  }
+  return worst + kLaunchKb;
+}
+
+// The SM budget is a preference: a launch keeps to `budget` SMs (leaving the
+// rest to collectives running beside it) unless all SMs would finish it
+// more than 3 % sooner.
+template <typename Cost>
+int pick_sms(int budget, int all, Cost cost) {
+  if (all <= budget) return budget;
+  return cost(all) * 103 < cost(budget) * 100 ? all : budget;
+}
+}  // namespace
+
+namespace {
 // Tensor maps (A hi, A lo, B hi, B lo) and kernel parameters of one GEMM,
 // with its column-sum counters zeroed on stream s.  kOk, or an error code.
 int tc_prepare(const TcLaunch& L, const SplitOperand& A, const SplitOperand& B,
@@ -1161,7 +1215,9 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   // Fewest CTAs that still finish the tiles in the same number of waves: a
   // 128- or 512-tile GEMM takes 128 SMs, leaving the rest to a concurrent
   // NCCL all-reduce at no cost to the GEMM (B200 has 148 SMs).
-  const int waves = (p.num_tiles + L.num_sms - 1) / L.num_sms;
+  const int G = L.all_sms > L.num_sms ? tc_launch_sms(M, N, K, L.num_sms, L.all_sms, passes)
+                                       : L.num_sms;
+  const int waves = (p.num_tiles + G - 1) / G;
   int grid = (p.num_tiles + waves - 1) / waves;
   static const bool dyn_enabled = [] {  // dynamic tile order: opt-in (MX_DYNSCHED=1)
     const char* e = std::getenv("MX_DYNSCHED");
@@ -1172,8 +1228,8 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
     cudaError_t me = cudaMemsetAsync(L.sched, 0, sizeof(int), s);
     if (me != cudaSuccess) return cuda_status(me);
   }
-  const SplitPlan sp = plan_split(M, N, K, L.num_sms, passes);
-  const size_t sk_need = tc_streamk_bytes(M, N, K, L.num_sms, passes);
+  const SplitPlan sp = plan_split(M, N, K, G, passes);
+  const size_t sk_need = tc_streamk_bytes(M, N, K, G, passes);
   if (sp.mode != 0 && L.ws && L.ws_bytes >= sk_need && !p.tile_counter) {
     p.sk = sp.mode;
     p.sk_tile0 = sp.tile0;  // full waves stay data-parallel
@@ -1185,7 +1241,7 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
     p.sk_partials = static_cast<float*>(L.ws);
     p.sk_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(L.ws) +
                                            sp.slots * kBM * kBN * 4);
-    grid = L.num_sms;
+    grid = G;
     cudaError_t me = cudaMemsetAsync(p.sk_counters, 0, sizeof(int) * p.num_tiles, s);
     if (me != cudaSuccess) return cuda_status(me);
   }
@@ -1210,55 +1266,6 @@ cudaError_t launch_pair(const CUtensorMap (&m0)[4], const CUtensorMap (&m1)[4],
   return cudaGetLastError();
 }
 
-// Cost model of the pair decision, in k-blocks of one CTA (3xTF32 stages):
-// a launch costs its prologue, pipeline fill and last unhidden epilogue
-// (kLaunchKb); a split tile costs the partial-tile round trip (kFinishKb).
-constexpr int64_t kLaunchKb = 48, kFinishKb = 32;
-
-int64_t tiles_of(int M, int N) {
-  return static_cast<int64_t>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-}
-
-// Busiest CTA of one launch of its own, as tc_gemm_split schedules it.
-int64_t single_makespan(const TcPairGemm& g, int num_sms) {
-  const int64_t tiles = tiles_of(g.M, g.N), kb = (g.K + kBK - 1) / kBK;
-  const SplitPlan sp = plan_split(g.M, g.N, g.K, num_sms, 3);
-  const int64_t full = tiles / num_sms;
-  if (sp.mode == 2) {
-    const int64_t helper = sp.s > 0 ? kb - sp.kp - static_cast<int64_t>(sp.s - 1) * sp.len
-                                    : static_cast<int64_t>(sp.j) * (kb - sp.kp);
-    return full * kb + std::max<int64_t>(sp.kp, helper) + kFinishKb + kLaunchKb;
-  }
-  if (sp.mode == 1)
-    return full * kb + ((tiles - full * num_sms) * kb + num_sms - 1) / num_sms + kFinishKb +
-           kLaunchKb;
-  return (tiles + num_sms - 1) / num_sms * kb + kLaunchKb;
-}
-
-// Busiest CTA of the paired launch: a's tiles, then b's, round robin.
-int64_t pair_makespan(const TcPairGemm& a, const TcPairGemm& b, int num_sms) {
-  const int64_t ta = tiles_of(a.M, a.N), tb = tiles_of(b.M, b.N);
-  const int64_t ka = (a.K + kBK - 1) / kBK, kbb = (b.K + kBK - 1) / kBK;
-  const int64_t G = std::min<int64_t>(num_sms, ta + tb);
-  int64_t worst = 0;
-  for (int64_t c = 0; c < G; ++c) {
-    const int64_t na = c < ta ? (ta - c + G - 1) / G : 0;
-    // b's tile u sits at index ta + u; CTA c takes those with (ta + u) % G == c
-    const int64_t first = ((c - ta) % G + G) % G;
-    const int64_t nb = first < tb ? (tb - first + G - 1) / G : 0;
-    worst = std::max(worst, na * ka + nb * kbb);
-  }
-  return worst + kLaunchKb;
-}
-
-bool pair_pays(const TcPairGemm& a, const TcPairGemm& b, int num_sms) {
-  static const bool forced = [] {  // MX_PAIR=0: always two launches
-    const char* e = std::getenv("MX_PAIR");
-    return e && e[0] == '0';
-  }();
-  if (forced) return false;
-  return pair_makespan(a, b, num_sms) <= single_makespan(a, num_sms) + single_makespan(b, num_sms);
-}
 }  // namespace
 
 int tc_gemm_pair(const TcLaunch& L, const TcPairGemm& g0, const TcPairGemm& g1, cudaStream_t s) {
@@ -1284,7 +1291,18 @@ int tc_gemm_pair(const TcLaunch& L, const TcPairGemm& g0, const TcPairGemm& g1, 
     const int rc = tc_gemm_split(L, g0.A, g0.B, g0.E, g0.M, g0.N, g0.K, 3, s);
     return rc != kOk ? rc : tc_gemm_split(L, g1.A, g1.B, g1.E, g1.M, g1.N, g1.K, 3, s);
   }
-  if (!pair_pays(a, b, L.num_sms)) {
+  // Paired or as two launches, on the budget's SMs or on all of them:
+  // whichever the cost model finishes first (MX_PAIR=0: always two launches).
+  static const bool pair_off = [] {
+    const char* e = std::getenv("MX_PAIR");
+    return e && e[0] == '0';
+  }();
+  auto separate = [&](int G) {
+    return gemm_makespan(a.M, a.N, a.K, G, 3) + gemm_makespan(b.M, b.N, b.K, G, 3);
+  };
+  auto best = [&](int G) { return std::min(pair_makespan(a, b, G), separate(G)); };
+  const int G = L.all_sms > L.num_sms ? pick_sms(L.num_sms, L.all_sms, best) : L.num_sms;
+  if (pair_off || pair_makespan(a, b, G) > separate(G)) {
     const int rc = tc_gemm_split(L, g0.A, g0.B, g0.E, g0.M, g0.N, g0.K, 3, s);
     return rc != kOk ? rc : tc_gemm_split(L, g1.A, g1.B, g1.E, g1.M, g1.N, g1.K, 3, s);
   }
@@ -1296,7 +1314,7 @@ int tc_gemm_pair(const TcLaunch& L, const TcPairGemm& g0, const TcPairGemm& g1, 
   if (rc != kOk) return rc;
   pa.pair_tiles = pb.num_tiles;
   const int total = pa.num_tiles + pb.num_tiles;
-  const int grid = std::min(L.num_sms, total);
+  const int grid = std::min(G, total);
   const cudaError_t e = fn(ma, mb, pa, pb, grid, s);
   return e == cudaSuccess ? kOk : cuda_status(e);
 }
@@ -1315,6 +1333,11 @@ void tc_split_plan(int M, int N, int K, int num_sms, int passes, int32_t* out) {
   out[3] = sp.kp;
   out[4] = sp.s;
   out[5] = sp.j;
+}
+
+int tc_launch_sms(int M, int N, int K, int budget, int all, int passes) {
+  if (M <= 0 || N <= 0 || K <= 0) return budget;
+  return pick_sms(budget, all, [&](int G) { return gemm_makespan(M, N, K, G, passes); });
 }
 
 size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes) {
@@ -1337,7 +1360,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
   if (passes != 1 && passes != 3) return kErrInvalid;
   const CopyShape ca = copy_shape(g.ta == 0, g.M, g.K), cb = copy_shape(g.tb != 0, g.N, g.K);
   const size_t split_bytes = tc_gemm_workspace_bytes(g, passes);
-  const size_t sk_bytes = tc_streamk_bytes(g.M, g.N, g.K, ctx->tc_sms(), passes);
+  const size_t sk_bytes = tc_split_scratch(ctx, g.M, g.N, g.K, passes);
   int rc = ensure_workspace(ctx, split_bytes + sk_bytes);
   if (rc != kOk) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->workspace);
@@ -1361,6 +1384,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
                 : launch_split(g.b, g.ldb, true, g.K, g.N, cb.ld, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
+  L.all_sms = ctx->num_sms;
   L.sched = ctx->sched;
   L.ws = static_cast<uint8_t*>(ctx->workspace) + split_bytes;  // split_bytes is 256-aligned
   L.ws_bytes = sk_bytes;

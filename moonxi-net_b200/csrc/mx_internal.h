@@ -32,9 +32,11 @@ struct Context {
   // no memset.  Calls that overlap on the GPU must not share a context.
   static constexpr int kCounters = 65536;
   int* counters = nullptr;
-  // SMs the tensor-core GEMMs may occupy (0: all).  A data-parallel step
-  // leaves the rest free so that NCCL kernels overlapping a GEMM find SMs
-  // (a persistent GEMM CTA and an NCCL CTA do not fit on one SM together).
+  // SMs the tensor-core GEMMs prefer to occupy (0: all).  A data-parallel
+  // step leaves the rest free so that NCCL kernels overlapping a GEMM find
+  // SMs (a persistent GEMM CTA and an NCCL CTA do not fit on one SM
+  // together); a launch still takes every SM when that finishes it more than
+  // 3 % sooner (tc_launch_sms).
   int sm_budget = 0;
   int tc_sms() const { return sm_budget > 0 && sm_budget < num_sms ? sm_budget : num_sms; }
 };
@@ -102,10 +104,20 @@ struct TcLaunch {
   // device int for dynamic whole-tile scheduling (zeroed per launch on the
   // launch stream), or null for a static tile order
   int* sched = nullptr;
+  // all SMs of the device; num_sms is then the preferred budget (0: num_sms)
+  int all_sms = 0;
 };
 // Scratch of the partial tiles a launch of this shape splits (stream-K or
 // tail split; 0: whole tiles only).
 size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes);
+// SMs a single tcgen05 GEMM launch of this shape uses: `budget`, or `all`
+// when all SMs finish it more than 3 % sooner (cost model in gemm_tc.cu).
+int tc_launch_sms(int M, int N, int K, int budget, int all, int passes);
+// Scratch of the partial tiles for a launch on context c.
+inline size_t tc_split_scratch(const Context* c, int M, int N, int K, int passes) {
+  return tc_streamk_bytes(M, N, K, tc_launch_sms(M, N, K, c->tc_sms(), c->num_sms, passes),
+                          passes);
+}
 // One operand in hi/lo split form (lo may be null for passes = 1).
 // kmajor: element (r, k) at hi[r * ld + k]; else at hi[k * ld + r].
 struct SplitOperand {

@@ -296,3 +296,33 @@ def test_gemm_split_pair_matches_two_launches(cuda_device, B, fi, fo, nt):
     want = paired["dx"].double().sum(0)
     assert float(((paired["cs"].double() - want).abs() /
                   paired["dx"].double().abs().sum(0).clamp_min(1e-30)).max()) <= 1e-6 * math.sqrt(B)
+
+
+def test_sm_budget_is_a_preference(cuda_device):
+    """With 128 of 148 SMs preferred, a GEMM whose tiles make whole 128-SM
+    waves keeps to the budget (whole tiles), while one that all SMs finish
+    clearly sooner (512 tiles: 3 waves and a split instead of 4 waves) takes
+    them, with its tail split."""
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    ctx = ops.new_context(0)
+    try:
+        ops.set_sm_budget(ctx, 128)
+        assert ops.split_plan(1024, 4096, 4096, ctx=ctx)["mode"] == 0
+        assert ops.split_plan(4096, 4096, 4096, ctx=ctx)["mode"] == 2
+        # and the GEMM computes the same either way
+        M = K = N = 2048
+        g = torch.Generator("cuda").manual_seed(5)
+        A = torch.randn(M, K, device="cuda", generator=g)
+        B = torch.randn(K, N, device="cuda", generator=g)
+        ah, al = _split(A)
+        bh, bl = _split(B)
+        c = torch.empty(M, N, device="cuda")
+        ops.gemm_split(ah, al, K, True, bh, bl, N, False, M, K, N, c=c, padded=3, ctx=ctx)
+        torch.cuda.synchronize()
+        assert ops.context_status(ctx)[0] == 0
+        ref = A.double() @ B.double()
+        scale = A.double().abs() @ B.double().abs()
+        assert float(((c.double() - ref).abs() / scale).max()) <= 1e-5 * math.sqrt(K)
+    finally:
+        ops.destroy_context(ctx)

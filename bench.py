@@ -181,7 +181,8 @@ def cpu_rate_sample(target_s: float):
     fixed, per_row, full = _fit_full_step(pts)
     return {"value": GLOBAL_BATCH / full, "unit": "samples/s", "cores": threads, "kind": "port",
             "sample": f"NpArray restatement, one fwd+bwd+SGD step at {small} and {large} rows "
-                      f"({pts[0][1]:.2f} s, {pts[1][1]:.2f} s); fitted fixed {fixed:.2f} s + "
+                      f"({pts[-2][1]:.2f} s, {pts[-1][1]:.2f} s; with the 8- and 40-row "
+                      f"calibration steps, 4 points); fitted fixed {fixed:.2f} s + "
                       f"{per_row * 1e3:.2f} ms/row, extrapolated to the {GLOBAL_BATCH}-row "
                       f"step ({full:.1f} s)",
             "fixed_s": round(fixed, 3), "per_row_ms": round(per_row * 1e3, 3),
@@ -760,6 +761,66 @@ def run_gemm_only(args):
     return 0
 
 
+def run_pair_only(args):
+    """One Linear layer's backward (layout nn: dX = dY W^T masked, with split
+    output and column sums; dW = X^T dY) through mx_gemm_split_pair, K timed
+    calls after W warm-ups (L2 flushed between calls); --pair B,FI,FO, with
+    --sm-budget S preferring S SMs as a data-parallel step does."""
+    import torch
+
+    from moonxi_net_b200 import ops
+    torch.cuda.set_device(0)
+    B, fi, fo = (int(v) for v in args.pair.split(","))
+    ctx = ops.new_context(0)
+    if args.sm_budget:
+        ops.set_sm_budget(ctx, args.sm_budget)
+
+    def split(rows, cols):
+        x = torch.randn(rows, cols, device="cuda")
+        hi = torch.empty(rows * cols + 64, device="cuda")
+        lo = torch.empty(rows * cols + 64, device="cuda")
+        ops.split_tf32(x, hi[:rows * cols].view(rows, cols), lo[:rows * cols].view(rows, cols),
+                       ctx=ctx)
+        return x, hi, lo
+    _, gh, gl = split(B, fo)       # dY
+    h, hh, hl = split(B, fi)       # layer input (its ReLU mask)
+    _, wh, wl = split(fi, fo)      # W [in, out]
+    dx, dx_hi, dx_lo = (torch.empty(B * fi, device="cuda") for _ in range(3))
+    dw = torch.empty(fi * fo, device="cuda")
+    cs = torch.empty(fi, device="cuda")
+    scratch = torch.empty(ops.gemm_colsum_scratch_bytes(B, fi) // 4, device="cuda")
+    dx_kw = dict(a_hi=gh, a_lo=gl, lda=fo, a_kmajor=True, b_hi=wh, b_lo=wl, ldb=fo,
+                 b_kmajor=True, M=B, K=fo, N=fi, c=dx, c_hi=dx_hi, c_lo=dx_lo, mask=h, ldm=fi,
+                 colsum=cs, colsum_scratch=scratch, padded=3)
+    dw_kw = dict(a_hi=hh, a_lo=hl, lda=fi, a_kmajor=False, b_hi=gh, b_lo=gl, ldb=fo,
+                 b_kmajor=False, M=fi, K=B, N=fo, c=dw, padded=3)
+    flush = torch.empty(int(256e6) // 4, device="cuda")
+    for _ in range(args.warmup):
+        ops.gemm_split_pair(dx_kw, dw_kw, ctx=ctx)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.gemm_split_pair(dx_kw, dw_kw, ctx=ctx)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    rc, where = ops.context_status(ctx)
+    ops.destroy_context(ctx)
+    if rc != 0:
+        print(f"status {rc} at call site {where}", file=sys.stderr)
+        return 1
+    t = statistics.median(times)
+    fl = 2.0 * 2 * B * fi * fo
+    print(json.dumps({"metric": f"layer backward pair B={B} {fi}->{fo}", "ms": t * 1e3,
+                      "tflops": fl / t / 1e12, "tf32_tflops_3x": 3 * fl / t / 1e12,
+                      "sm_budget": args.sm_budget, "steps": args.steps,
+                      "warmup": args.warmup}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -783,10 +844,16 @@ def main():
     ap.add_argument("--layout", default="nn", choices=["nn", "nt", "tn"])
     ap.add_argument("--shape", default="", metavar="M,K,N",
                     help="time only this GEMM (any shape; default precision auto)")
+    ap.add_argument("--pair", default="", metavar="B,FI,FO",
+                    help="time only one Linear layer's paired backward GEMMs")
+    ap.add_argument("--sm-budget", type=int, default=0,
+                    help="with --pair: SMs the GEMMs prefer (a data-parallel step's 128)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps
     if args.impl == "reference":
         return run_reference(args)
+    if args.pair:
+        return run_pair_only(args)
     if args.gemm or args.shape:
         return run_gemm_only(args)
     return run_ours(args)

@@ -335,20 +335,34 @@ __device__ __forceinline__ void store_rows(const TcParams& p, int row0, int col,
 }
 
 // Epilogue of four consecutive outputs (row, col..col+3): the same math as
-// store_rows for a 4-wide group.
+// store_rows for a 4-wide group; b4 holds bias[col..col+3] (zero past N),
+// loaded once by the caller.
 __device__ __forceinline__ float4 store_quad(const TcParams& p, int row, int col, float4 acc,
-                                             bool vec_ok, bool mask_vec) {
+                                             float4 b4, bool vec_ok, bool mask_vec) {
   const int64_t roff = static_cast<int64_t>(row) * p.ldc;
   const bool full = col + 4 <= p.N;
+  float m[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+  if (p.mask) {
+    const float* mp = p.mask + static_cast<int64_t>(row) * p.ldm + col;
+    if (mask_vec && full) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(mp));
+      m[0] = t.x; m[1] = t.y; m[2] = t.z; m[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (col + j < p.N) m[j] = __ldg(mp + j);
+    }
+  }
   float v[4] = {acc.x, acc.y, acc.z, acc.w};
+  const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float x = p.alpha * v[j];
     if (col + j < p.N) {
       if (p.beta != 0.0f) x = x + p.beta * p.c[roff + col + j];
-      if (p.bias) x = x + __ldg(p.bias + col + j);
+      if (p.bias) x = x + bb[j];
       if (p.relu) x = x > 0.0f ? x : 0.0f;
-      if (p.mask && !(__ldg(p.mask + static_cast<int64_t>(row) * p.ldm + col + j) > 0.0f)) x = 0.0f;
+      if (p.mask && !(m[j] > 0.0f)) x = 0.0f;
     }
     v[j] = x;
   }
@@ -378,7 +392,6 @@ __device__ __forceinline__ float4 store_quad(const TcParams& p, int row, int col
         }
       }
   }
-  (void)mask_vec;
   return make_float4(v[0], v[1], v[2], v[3]);  // the stored values, for column sums
 }
 
@@ -769,32 +782,60 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
           const int q = row_in_tile & 63;
           const int64_t tile_off = static_cast<int64_t>(row_in_tile >> 6) * kBN + q * 4;
           const int col = tn * kBN + q * 4;
+          float4 b4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // bias of my four columns
+          if (p.bias && col < p.N) {
+            b4.x = __ldg(p.bias + col);
+            if (col + 1 < p.N) b4.y = __ldg(p.bias + col + 1);
+            if (col + 2 < p.N) b4.z = __ldg(p.bias + col + 2);
+            if (col + 3 < p.N) b4.w = __ldg(p.bias + col + 3);
+          }
+          auto part_src = [&](int j, int i0) {
+            return p.sk_partials + part_slot(p, t, num_kb, c_first, j) * (kBM * kBN) + tile_off +
+                   static_cast<int64_t>(i0) * 2 * kBN;
+          };
+          auto add8 = [](float4 (&acc)[8], const float4 (&v)[8]) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              acc[u].x += v[u].x;
+              acc[u].y += v[u].y;
+              acc[u].z += v[u].z;
+              acc[u].w += v[u].w;
+            }
+          };
           float4 cs = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // column sums of my rows
 #pragma unroll 1
           for (int i0 = 0; i0 < kBM / 2; i0 += 8) {
             float4 s[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) s[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int j = 0; j < parts; ++j) {  // k order: same sum on any finisher
-              const float* src = p.sk_partials + part_slot(p, t, num_kb, c_first, j) * (kBM * kBN) +
-                                 tile_off + static_cast<int64_t>(i0) * 2 * kBN;
-              float4 v[8];
+            // k order (same sum on any finisher), two parts' loads in flight
+            int j = 0;
+            for (; j + 2 <= parts; j += 2) {
+              const float* s0 = part_src(j, i0);
+              const float* s1 = part_src(j + 1, i0);
+              float4 v0[8], v1[8];
 #pragma unroll
               for (int u = 0; u < 8; ++u)
-                v[u] = __ldcg(reinterpret_cast<const float4*>(src + u * 2 * kBN));
+                v0[u] = __ldcg(reinterpret_cast<const float4*>(s0 + u * 2 * kBN));
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                s[u].x += v[u].x;
-                s[u].y += v[u].y;
-                s[u].z += v[u].z;
-                s[u].w += v[u].w;
-              }
+              for (int u = 0; u < 8; ++u)
+                v1[u] = __ldcg(reinterpret_cast<const float4*>(s1 + u * 2 * kBN));
+              add8(s, v0);
+              add8(s, v1);
+            }
+            if (j < parts) {
+              const float* s0 = part_src(j, i0);
+              float4 v0[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                v0[u] = __ldcg(reinterpret_cast<const float4*>(s0 + u * 2 * kBN));
+              add8(s, v0);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int r = tm * kBM + (row_in_tile >> 6) + 2 * (i0 + u);
               if (r < p.M && col < p.N) {
-                const float4 o = store_quad(p, r, col, s[u], vec_ok, mask_vec);
+                const float4 o = store_quad(p, r, col, s[u], b4, vec_ok, mask_vec);
                 cs.x += o.x;
                 cs.y += col + 1 < p.N ? o.y : 0.0f;
                 cs.z += col + 2 < p.N ? o.z : 0.0f;

@@ -272,10 +272,16 @@ void* mx_context_create(int32_t device);
 void mx_context_destroy(void* handle);
 int32_t mx_context_set_stream(void* handle, void* stream);
 int32_t mx_context_set_precision(void* handle, int32_t precision);
-/* SMs this context's tensor-core GEMMs may occupy (0 = all).  A
+/* SMs this context's tensor-core GEMMs prefer to occupy (0 = all).  A
  * data-parallel step sets it below the SM count so that collectives
- * launched on another stream find free SMs while a GEMM runs. */
+ * launched on another stream find free SMs while a GEMM runs; a launch still
+ * takes every SM (up to the limit below) when that finishes it more than 3 %
+ * sooner. */
 int32_t mx_context_set_sm_budget(void* handle, int32_t sms);
+/* Hard cap on the SMs of this context's tensor-core GEMMs (0 = none): for a
+ * step whose collectives must overlap every GEMM (the weight all-gathers of
+ * a sharded update run beside the forward GEMMs that need them). */
+int32_t mx_context_set_sm_limit(void* handle, int32_t sms);
 /* Bound (nanoseconds) on every in-kernel wait; default 2 s. */
 int32_t mx_context_set_timeout_ns(void* handle, uint64_t ns);
 /* Pre-sizes the context workspace (split operands, split-K partials) so that
@@ -403,6 +409,13 @@ int32_t moonbit_nccl_get_unique_id(uint8_t* id);
  * the reason in moonbit_nccl_last_status().  Like the reference's
  * moonbit_cublas_create (cuda_stub.c:240-242), the handle is a plain void*. */
 void* moonbit_nccl_init(const uint8_t* id, int32_t rank, int32_t world, int32_t device);
+/* moonbit_nccl_init with a cap on the CTAs (SMs) each of the communicator's
+ * collectives may take (max_ctas = 0: NCCL's default).  A data-parallel step
+ * whose GEMMs leave S SMs free passes S, so that a collective overlapping a
+ * GEMM runs all of its channels at once instead of waiting for the GEMM to
+ * release SMs (NCCL's ncclCommInitRankConfig, maxCTAs). */
+void* moonbit_nccl_init_ex(const uint8_t* id, int32_t rank, int32_t world, int32_t device,
+                           int32_t max_ctas);
 /* moonbit_nccl_init with a file as the side channel, for hosts that have no
  * other: rank 0 writes a fresh id to `path` (written to a temporary name and
  * renamed, so readers never see part of it), the other ranks wait up to

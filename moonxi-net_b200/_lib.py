@@ -94,6 +94,7 @@ SIGNATURES = {
     "mx_context_set_precision": (_i32, [_vp, _i32]),
     "mx_context_set_timeout_ns": (_i32, [_vp, ctypes.c_uint64]),
     "mx_context_set_sm_budget": (_i32, [_vp, _i32]),
+    "mx_context_set_sm_limit": (_i32, [_vp, _i32]),
     "mx_context_reserve_workspace": (_i32, [_vp, ctypes.c_uint64]),
     "mx_matmul_workspace_bytes": (ctypes.c_uint64, [_vp, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mx_context_status": (_i32, [_vp, ctypes.POINTER(_i32)]),
@@ -110,6 +111,7 @@ SIGNATURES = {
     "moonbit_nccl_version": (_i32, []),
     "moonbit_nccl_get_unique_id": (_i32, [_vp]),
     "moonbit_nccl_init": (_vp, [_vp, _i32, _i32, _i32]),
+    "moonbit_nccl_init_ex": (_vp, [_vp, _i32, _i32, _i32, _i32]),
     "moonbit_nccl_init_file": (_vp, [ctypes.c_char_p, _i32, _i32, _i32, _i32]),
     "moonbit_nccl_last_status": (_i32, []),
     "moonbit_nccl_comm_info": (_i32, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32),

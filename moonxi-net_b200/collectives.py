@@ -62,7 +62,10 @@ class NcclCollectives:
         self.stream = torch.cuda.Stream(device=device)
 
     @classmethod
-    def from_process_group(cls, group, device: torch.device) -> "NcclCollectives":
+    def from_process_group(cls, group, device: torch.device,
+                           max_ctas: int = 0) -> "NcclCollectives":
+        """max_ctas > 0: each collective takes at most that many SMs
+        (moonbit_nccl_init_ex), so that it fits beside GEMMs leaving them free."""
         import torch.distributed as dist
         L = _lib.lib()
         rank = dist.get_rank(group)
@@ -75,9 +78,9 @@ class NcclCollectives:
         src = dist.get_global_rank(group, 0) if group is not None else 0
         dist.broadcast_object_list(obj, src=src, group=group)
         idbuf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES).from_buffer_copy(obj[0])
-        h = L.moonbit_nccl_init(idbuf, rank, world, device.index)
+        h = L.moonbit_nccl_init_ex(idbuf, rank, world, device.index, int(max_ctas))
         if not h:
-            raise _lib.MXError(L.moonbit_nccl_last_status(), "moonbit_nccl_init")
+            raise _lib.MXError(L.moonbit_nccl_last_status(), "moonbit_nccl_init_ex")
         return cls(h, device)
 
     # -- the collectives (sum over ranks, fp32, in place where the step needs)
@@ -160,13 +163,14 @@ class TorchCollectives:
         return None
 
 
-def as_collectives(group, device=None):
-    """The collectives object for `group` (see the module docstring)."""
+def as_collectives(group, device=None, max_ctas: int = 0):
+    """The collectives object for `group` (see the module docstring);
+    max_ctas caps the SMs of each NCCL collective (0: NCCL's default)."""
     if isinstance(group, (NcclCollectives, TorchCollectives)):
         return group
     import torch.distributed as dist
     if group is not None or dist.is_initialized():
         backend = dist.get_backend(group)
         if str(backend).lower() == "nccl" and device is not None:
-            return NcclCollectives.from_process_group(group, device)
+            return NcclCollectives.from_process_group(group, device, max_ctas)
     return TorchCollectives(group)

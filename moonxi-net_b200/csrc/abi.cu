@@ -403,7 +403,7 @@ int gemm_split(void* handle, const float* a_hi, const float* a_lo, int64_t lda, 
   if (mask && ldm < N) return MX_ERR_INVALID;
   if (!c_hi && c_lo) return MX_ERR_INVALID;
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
-  L.all_sms = ctx->num_sms;
+  L.all_sms = ctx->tc_all();
   L.sched = ctx->sched;
   const size_t sk = tc_split_scratch(ctx, M, N, K, passes);
   if (sk > 0 && ensure_workspace(ctx, sk) == kOk) {
@@ -487,7 +487,7 @@ MX_EXPORT int32_t mx_gemm_split_pair(void* handle, const mx_split_gemm* g0,
   if (rc == kOk) rc = pair_gemm(g1, b);
   if (rc != kOk) return rc;
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
-  L.all_sms = ctx->num_sms;
+  L.all_sms = ctx->tc_all();
   // a layout pair without a paired kernel runs as two launches, which may
   // split K and then need the stream-K scratch
   const size_t sk = std::max(tc_split_scratch(ctx, a.M, a.N, a.K, 3),
@@ -506,7 +506,7 @@ MX_EXPORT int32_t mx_tc_split_plan(void* handle, int32_t M, int32_t N, int32_t K
   Context* ctx = scope.c;
   if (!ctx) return MX_ERR_NO_DEVICE;
   if (!out || M < 1 || N < 1 || K < 1 || (passes != 1 && passes != 3)) return MX_ERR_INVALID;
-  tc_split_plan(M, N, K, tc_launch_sms(M, N, K, ctx->tc_sms(), ctx->num_sms, passes),
+  tc_split_plan(M, N, K, tc_launch_sms(M, N, K, ctx->tc_sms(), ctx->tc_all(), passes),
                 passes, out);
   return MX_OK;
 }
@@ -578,6 +578,15 @@ MX_EXPORT int32_t mx_context_set_sm_budget(void* handle, int32_t sms) {
   if (!c) return MX_ERR_NO_DEVICE;
   if (sms < 0) return MX_ERR_INVALID;
   c->sm_budget = sms;
+  return MX_OK;
+}
+
+MX_EXPORT int32_t mx_context_set_sm_limit(void* handle, int32_t sms) {
+  Scoped scope(handle);
+  Context* c = scope.c;
+  if (!c) return MX_ERR_NO_DEVICE;
+  if (sms < 0) return MX_ERR_INVALID;
+  c->sm_limit = sms;
   return MX_OK;
 }
 

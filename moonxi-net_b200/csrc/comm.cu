@@ -37,6 +37,9 @@ struct NcclApi {
   ncclResult_t (*get_version)(int*) = nullptr;
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  // optional (NCCL >= 2.14): communicator options such as the CTA cap
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int,
+                                        ncclConfig_t*) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
   ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
@@ -76,6 +79,8 @@ const NcclApi& nccl() {
     MX_NCCL_SYM(comm_abort, "ncclCommAbort");
     MX_NCCL_SYM(comm_finalize, "ncclCommFinalize");
     MX_NCCL_SYM(comm_destroy, "ncclCommDestroy");
+    api.comm_init_rank_config = reinterpret_cast<decltype(api.comm_init_rank_config)>(
+        sym("ncclCommInitRankConfig"));
 #undef MX_NCCL_SYM
     api.ok = api.get_version && api.get_unique_id && api.comm_init_rank && api.all_reduce &&
              api.reduce_scatter && api.all_gather && api.broadcast && api.group_start &&
@@ -141,7 +146,9 @@ struct DeviceScope {
   }
 };
 
-void* init_with_id(const ncclUniqueId& id, int rank, int world, int device) {
+// max_ctas > 0: NCCL's kernels of this communicator take at most that many
+// CTAs (SMs), so that they fit beside GEMMs that leave that many SMs free.
+void* init_with_id(const ncclUniqueId& id, int rank, int world, int device, int max_ctas = 0) {
   const NcclApi& api = nccl();
   if (!api.ok) return fail(MX_ERR_UNSUPPORTED);
   int count = 0;
@@ -150,7 +157,16 @@ void* init_with_id(const ncclUniqueId& id, int rank, int world, int device) {
   DeviceScope ds(device);
   if (!ds.ok) return fail(MX_ERR_CUDA);
   ncclComm_t comm = nullptr;
-  ncclResult_t r = api.comm_init_rank(&comm, world, id, rank);
+  ncclResult_t r;
+  if (max_ctas > 0 && api.comm_init_rank_config) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.minCTAs = 1;
+    cfg.maxCTAs = max_ctas;
+    r = api.comm_init_rank_config(&comm, world, id, rank, &cfg);
+  } else {
+    if (max_ctas > 0) return fail(MX_ERR_UNSUPPORTED);
+    r = api.comm_init_rank(&comm, world, id, rank);
+  }
   if (r != ncclSuccess) return fail(nccl_status(r));
   Comm* c = new Comm();
   c->comm = comm;
@@ -196,6 +212,14 @@ MX_EXPORT void* moonbit_nccl_init(const uint8_t* id, int32_t rank, int32_t world
   ncclUniqueId u;
   std::memcpy(u.internal, id, MX_NCCL_UNIQUE_ID_BYTES);
   return init_with_id(u, rank, world, device);
+}
+
+MX_EXPORT void* moonbit_nccl_init_ex(const uint8_t* id, int32_t rank, int32_t world,
+                                     int32_t device, int32_t max_ctas) {
+  if (!id || world < 1 || rank < 0 || rank >= world || max_ctas < 0) return fail(MX_ERR_INVALID);
+  ncclUniqueId u;
+  std::memcpy(u.internal, id, MX_NCCL_UNIQUE_ID_BYTES);
+  return init_with_id(u, rank, world, device, max_ctas);
 }
 
 MX_EXPORT void* moonbit_nccl_init_file(const char* path, int32_t rank, int32_t world,

@@ -1425,7 +1425,7 @@ int tc_gemm(Context* ctx, const GemmArgs& g, int passes, cudaStream_t s) {
                 : launch_split(g.b, g.ldb, true, g.K, g.N, cb.ld, b_hi, b_lo, ctx->num_sms, s);
   if (e != cudaSuccess) return cuda_status(e);
   TcLaunch L{ctx->tc_sms(), ctx->status, ctx->timeout_ns};
-  L.all_sms = ctx->num_sms;
+  L.all_sms = ctx->tc_all();
   L.sched = ctx->sched;
   L.ws = static_cast<uint8_t*>(ctx->workspace) + split_bytes;  // split_bytes is 256-aligned
   L.ws_bytes = sk_bytes;

@@ -38,7 +38,10 @@ struct Context {
   // together); a launch still takes every SM when that finishes it more than
   // 3 % sooner (tc_launch_sms).
   int sm_budget = 0;
-  int tc_sms() const { return sm_budget > 0 && sm_budget < num_sms ? sm_budget : num_sms; }
+  // Hard cap on those SMs (0: none).
+  int sm_limit = 0;
+  int tc_all() const { return sm_limit > 0 && sm_limit < num_sms ? sm_limit : num_sms; }
+  int tc_sms() const { return sm_budget > 0 && sm_budget < tc_all() ? sm_budget : tc_all(); }
 };
 
 // One GEMM as the reference defines it (cuda_kernels.cu:1444-1499), with the
@@ -115,7 +118,7 @@ size_t tc_streamk_bytes(int M, int N, int K, int num_sms, int passes);
 int tc_launch_sms(int M, int N, int K, int budget, int all, int passes);
 // Scratch of the partial tiles for a launch on context c.
 inline size_t tc_split_scratch(const Context* c, int M, int N, int K, int passes) {
-  return tc_streamk_bytes(M, N, K, tc_launch_sms(M, N, K, c->tc_sms(), c->num_sms, passes),
+  return tc_streamk_bytes(M, N, K, tc_launch_sms(M, N, K, c->tc_sms(), c->tc_all(), passes),
                           passes);
 }
 // One operand in hi/lo split form (lo may be null for passes = 1).

@@ -178,6 +178,13 @@ class MLP:
         # an NCCL group, torch.distributed otherwise), "torch" = always
         # torch.distributed, or a collectives object to share
         self.coll = None
+        # SMs left to the collectives that overlap the GEMMs (a persistent GEMM
+        # CTA and an NCCL CTA do not fit on one SM together): the GEMMs prefer
+        # the rest (on 148 SMs the 128 left also make every power-of-two tile
+        # count a whole number of waves) and each NCCL collective is capped to
+        # them, so that all its channels run at once beside a GEMM
+        import os
+        self.comm_sms = int(os.environ.get("MX_COMM_SMS", "20"))
         if process_group is not None:
             import torch.distributed as dist
             self.world = dist.get_world_size(process_group)
@@ -188,18 +195,14 @@ class MLP:
             elif collectives is not None:
                 self.coll = collectives
             else:
-                self.coll = as_collectives(process_group, self.device)
+                self.coll = as_collectives(process_group, self.device,
+                                           max_ctas=self.comm_sms if self.world > 1 else 0)
         else:
             self.world = 1
         self._owns_coll = collectives is None and self.coll is not None
         if self.world > 1:
-            # leave SMs to the collectives that overlap the backward GEMMs: a
-            # persistent GEMM CTA and an NCCL CTA do not fit on one SM together
-            # (on 148 SMs the 128 left also make every power-of-two tile count
-            # a whole number of waves)
-            import os
             sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-            ops.set_sm_budget(self.ctx, sms - int(os.environ.get("MX_COMM_SMS", "20")))
+            ops.set_sm_budget(self.ctx, sms - self.comm_sms)
         # Split-form path (3xTF32 with every operand kept as hi/lo copies written
         # by its producer): needs TMA-legal leading dimensions (multiples of 4).
         self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
@@ -213,6 +216,11 @@ class MLP:
         # update halves, the forward grows by the gather and the re-split),
         # so the default stays all-reduce + replicated update.
         self.sharded = self.fused and self.world > 1 and bool(shard_update)
+        if self.sharded:
+            # the weight all-gathers run beside the forward GEMMs that need
+            # them: those GEMMs must leave the collectives their SMs
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            ops.set_sm_limit(self.ctx, sms - self.comm_sms)
 
         self.layout_ = FlatLayout(self.dims, self.world if self.sharded else 1)
         self.w_off, self.b_off = self.layout_.w_off, self.layout_.b_off

@@ -51,8 +51,14 @@ def destroy_context(h) -> None:
 
 
 def set_sm_budget(ctx, sms: int) -> None:
-    """SMs the context's tensor-core GEMMs may occupy (0 = all)."""
+    """SMs the context's tensor-core GEMMs prefer (0 = all); a launch takes
+    every SM when that finishes it more than 3 % sooner."""
     check(_lib.lib().mx_context_set_sm_budget(ctx, int(sms)), "mx_context_set_sm_budget")
+
+
+def set_sm_limit(ctx, sms: int) -> None:
+    """Hard cap on the SMs of the context's tensor-core GEMMs (0 = none)."""
+    check(_lib.lib().mx_context_set_sm_limit(ctx, int(sms)), "mx_context_set_sm_limit")
 
 
 def _handle(ctx, t: torch.Tensor) -> int:

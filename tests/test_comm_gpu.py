@@ -64,6 +64,28 @@ def test_one_rank_collectives(cuda_device):
         assert L.moonbit_nccl_destroy(h) == _lib.MX_ERR_INVALID  # gone
 
 
+def test_one_rank_comm_with_cta_cap(cuda_device):
+    """moonbit_nccl_init_ex: a communicator whose collectives take at most 8
+    SMs (NCCL's maxCTAs) computes the same all-reduce; a negative cap is an
+    argument error."""
+    L = _lib.lib()
+    buf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES)()
+    assert L.moonbit_nccl_get_unique_id(buf) == 0
+    assert not L.moonbit_nccl_init_ex(buf, 0, 1, 0, -1)
+    assert L.moonbit_nccl_last_status() == _lib.MX_ERR_INVALID
+    h = L.moonbit_nccl_init_ex(buf, 0, 1, 0, 8)
+    assert h, _lib.lib().mx_status_string(L.moonbit_nccl_last_status())
+    s = torch.cuda.Stream()
+    x = torch.randn(1 << 20, device="cuda")
+    y = torch.empty_like(x)
+    torch.cuda.synchronize()
+    assert L.moonbit_nccl_allreduce_sum_f32(h, x.data_ptr(), y.data_ptr(), x.numel(),
+                                            s.cuda_stream) == 0
+    assert L.moonbit_nccl_wait(h, s.cuda_stream, 10_000) == _lib.MX_OK
+    assert torch.equal(x, y)
+    assert L.moonbit_nccl_destroy(h) == 0
+
+
 def test_watchdog_times_out_and_aborts(cuda_device):
     """The stream is held by torch's bounded spin kernel (about half a
     second): the watchdog gives up after 50 ms, aborts the communicator (no

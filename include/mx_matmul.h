@@ -413,7 +413,8 @@ void* moonbit_nccl_init(const uint8_t* id, int32_t rank, int32_t world, int32_t 
  * collectives may take (max_ctas = 0: NCCL's default).  A data-parallel step
  * whose GEMMs leave S SMs free passes S, so that a collective overlapping a
  * GEMM runs all of its channels at once instead of waiting for the GEMM to
- * release SMs (NCCL's ncclCommInitRankConfig, maxCTAs). */
+ * release SMs (NCCL's ncclCommInitRankConfig: maxCTAs, and cgaClusterSize 1
+ * so that no launch needs several free SMs of one GPC at once). */
 void* moonbit_nccl_init_ex(const uint8_t* id, int32_t rank, int32_t world, int32_t device,
                            int32_t max_ctas);
 /* moonbit_nccl_init with a file as the side channel, for hosts that have no

@@ -147,7 +147,8 @@ struct DeviceScope {
 };
 
 // max_ctas > 0: NCCL's kernels of this communicator take at most that many
-// CTAs (SMs), so that they fit beside GEMMs that leave that many SMs free.
+// CTAs (SMs), launched without thread-block clusters, so that they fit beside
+// GEMMs that leave that many SMs free.
 void* init_with_id(const ncclUniqueId& id, int rank, int world, int device, int max_ctas = 0) {
   const NcclApi& api = nccl();
   if (!api.ok) return fail(MX_ERR_UNSUPPORTED);
@@ -162,6 +163,9 @@ void* init_with_id(const ncclUniqueId& id, int rank, int world, int device, int 
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.minCTAs = 1;
     cfg.maxCTAs = max_ctas;
+    // single-CTA launches: a cluster needs several SMs of one GPC free at
+    // once, which SMs left over here and there beside a GEMM rarely are
+    cfg.cgaClusterSize = 1;
     r = api.comm_init_rank_config(&comm, world, id, rank, &cfg);
   } else {
     if (max_ctas > 0) return fail(MX_ERR_UNSUPPORTED);

@@ -273,6 +273,9 @@ class MLP:
         # the exposed tail (the chunked GEMMs lose more than the overlap
         # gains), so one chunk is the default
         self.last_bucket_chunks = 1
+        # sharded update: the first layer's weights were gathered at the end
+        # of the last step
+        self._gathered0 = False
         # each hidden layer's backward GEMMs (dX and dW) as one paired launch
         self.pair_backward = pair_backward is not False
 
@@ -312,9 +315,10 @@ class MLP:
         """Sharded update only (a collective: every rank calls it): gathers
         every rank's pieces of the parameters (and of the velocities when
         asked) so that each replica holds the full state, e.g. before reading
-        or saving it.  The step itself gathers the weights it needs at its
-        start; between steps a rank's buffers are current only on its own
-        pieces.  No-op otherwise."""
+        or saving it.  The step itself gathers the weights it needs (the
+        first layer's at the end of the previous step, the others at its
+        start); between steps a rank's buffers are current only on its own
+        pieces and the first layer.  No-op otherwise."""
         if not self.sharded:
             return
         bufs = [self._params_full] + ([self._vels_full] if vels else [])
@@ -478,13 +482,16 @@ class MLP:
         if plan is not None:
             # the new weights: every rank's pieces, layer by layer, on the
             # collective stream while the forward of the earlier layers runs
-            gathers = [self._gather_layer(i) for i in range(self.L)]
+            # (the first layer's already came in at the end of the last step)
+            gathers = [None if (i == 0 and self._gathered0) else self._gather_layer(i)
+                       for i in range(self.L)]
+            self._gathered0 = False
         xh, xl = hsplit[0]
         ops.split_tf32(x, xh, xl, ctx=ctx)
         # forward: h_{i+1} = relu(h_i W_i + b_i); split copy written by the epilogue
         for i in range(self.L):
             last = i + 1 == self.L
-            if plan is not None:
+            if plan is not None and gathers[i] is not None:
                 gathers[i].wait()
                 if not self._split_on_coll_stream:
                     ops.split_tf32(self.w[i], self.w_hi[i], self.w_lo[i], ctx=ctx)
@@ -598,8 +605,11 @@ class MLP:
     def _sharded_update(self, update):
         """Global norm from every rank's gradient pieces (one small
         all-reduce that also sums the loss), then the update of this rank's
-        pieces.  The new split copies are made after the next step's
-        all-gather, so the update writes p and v only."""
+        pieces.  The first layer's new weights are all-gathered (and
+        re-split) right after its piece is updated, beside the update of the
+        other pieces: the next step's first GEMM needs them before anything
+        else could hide the gather.  The other layers' weights are gathered
+        at the next step's start, beside its forward."""
         ranges = self.plan.update_ranges()
         sc = self.scalars
         if ranges:
@@ -608,12 +618,22 @@ class MLP:
         else:
             ops.sum_squares(self.grads_buf[:0], sc[0:1], ctx=self.ctx)
         self.coll.all_reduce(sc).wait()
-        if update:
-            for a, b in ranges:
+        if not update:
+            return
+        g0 = None
+        for i, (a, b) in enumerate(self.plan.pieces):
+            a = max(a, _LOSS_SLOTS)
+            if b > a:
                 ops.sgd_momentum_clip(self._params_full[a:b], self.grads_buf[a:b],
                                       self._vels_full[a:b], self.lr, self.momentum,
                                       self.weight_decay, self.max_grad_norm, sc[0:1],
                                       ctx=self.ctx)
+            if i == 0:
+                g0 = self._gather_layer(0)
+        g0.wait()
+        if not self._split_on_coll_stream:
+            ops.split_tf32(self.w[0], self.w_hi[0], self.w_lo[0], ctx=self.ctx)
+        self._gathered0 = True
 
     # ------------------------------------------------------------ CUDA graph
     def capture(self, x: torch.Tensor, labels: torch.Tensor, global_batch: int | None = None):

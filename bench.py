@@ -829,10 +829,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32", "auto"])
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--shard-update", action="store_true",
+    ap.add_argument("--shard-update", dest="shard_update", action="store_const", const=True,
+                    default=None,
                     help="N>1: reduce-scatter the gradients, update 1/N of the parameters "
-                         "per rank, all-gather the weights (default: all-reduce, replicated "
-                         "update)")
+                         "per rank, all-gather the weights (the model's default from 4 GPUs)")
+    ap.add_argument("--replicated-update", dest="shard_update", action="store_const",
+                    const=False,
+                    help="N>1: all-reduce the gradients and update every parameter on every "
+                         "rank (the model's default on 2 GPUs)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--skip-configs", action="store_true",

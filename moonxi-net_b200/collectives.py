@@ -52,8 +52,11 @@ class NcclCollectives:
     broadcasts its 128 bytes (torch.distributed is used only for this
     bootstrap), every rank calls ``moonbit_nccl_init``."""
 
-    def __init__(self, handle: int, device: torch.device):
+    def __init__(self, handle: int, device: torch.device, full_handle: int | None = None):
         self.handle = handle
+        # optional second communicator without the CTA cap, for collectives
+        # that nothing overlaps (overlap=False): those may take every SM
+        self.full_handle = full_handle
         self.device = device
         r, w, d = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
         check(_lib.lib().moonbit_nccl_comm_info(handle, ctypes.byref(r), ctypes.byref(w),
@@ -64,76 +67,105 @@ class NcclCollectives:
     @classmethod
     def from_process_group(cls, group, device: torch.device,
                            max_ctas: int = 0) -> "NcclCollectives":
-        """max_ctas > 0: each collective takes at most that many SMs
-        (moonbit_nccl_init_ex), so that it fits beside GEMMs leaving them free."""
+        """max_ctas > 0: each collective that overlaps compute takes at most
+        that many SMs (moonbit_nccl_init_ex), so that it fits beside GEMMs
+        leaving them free; a second, uncapped communicator serves the
+        collectives that nothing overlaps."""
         import torch.distributed as dist
         L = _lib.lib()
         rank = dist.get_rank(group)
         world = dist.get_world_size(group)
+        n_comms = 2 if max_ctas > 0 else 1
         obj = [None]
         if rank == 0:
-            buf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES)()
-            check(L.moonbit_nccl_get_unique_id(buf), "moonbit_nccl_get_unique_id")
-            obj[0] = bytes(buf)
+            ids = []
+            for _ in range(n_comms):
+                buf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES)()
+                check(L.moonbit_nccl_get_unique_id(buf), "moonbit_nccl_get_unique_id")
+                ids.append(bytes(buf))
+            obj[0] = ids
         src = dist.get_global_rank(group, 0) if group is not None else 0
         dist.broadcast_object_list(obj, src=src, group=group)
-        idbuf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES).from_buffer_copy(obj[0])
-        h = L.moonbit_nccl_init_ex(idbuf, rank, world, device.index, int(max_ctas))
-        if not h:
-            raise _lib.MXError(L.moonbit_nccl_last_status(), "moonbit_nccl_init_ex")
-        return cls(h, device)
+        handles = []
+        for k, raw in enumerate(obj[0]):
+            idbuf = (ctypes.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES).from_buffer_copy(raw)
+            h = L.moonbit_nccl_init_ex(idbuf, rank, world, device.index,
+                                       int(max_ctas) if k == 0 else 0)
+            if not h:
+                st = L.moonbit_nccl_last_status()
+                for done in handles:
+                    L.moonbit_nccl_destroy(done)
+                raise _lib.MXError(st, "moonbit_nccl_init_ex")
+            handles.append(h)
+        return cls(handles[0], device, handles[1] if len(handles) > 1 else None)
 
     # -- the collectives (sum over ranks, fp32, in place where the step needs)
-    def _enqueue(self, fn, *args):
+    def _enqueue(self, fn, *args, overlap: bool = True):
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
-        check(fn(self.handle, *args, self.stream.cuda_stream), fn.__name__)
+        h = self.handle if (overlap or not self.full_handle) else self.full_handle
+        check(fn(h, *args, self.stream.cuda_stream), fn.__name__)
         ev = torch.cuda.Event()
         ev.record(self.stream)
         return _EventWork(ev)
 
-    def all_reduce(self, t: torch.Tensor, async_op: bool = True):
+    def all_reduce(self, t: torch.Tensor, async_op: bool = True, overlap: bool = True):
+        """overlap=False: nothing runs beside it (the uncapped communicator)."""
         w = self._enqueue(_lib.lib().moonbit_nccl_allreduce_sum_f32, t.data_ptr(), t.data_ptr(),
-                          t.numel())
+                          t.numel(), overlap=overlap)
         if not async_op:
             w.wait()
         return w
 
-    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = True):
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = True,
+                       overlap: bool = True):
         """out (this rank's piece) = sum over ranks of inp's piece; in place
         when out is inp's rank-th piece."""
         w = self._enqueue(_lib.lib().moonbit_nccl_reduce_scatter_sum_f32, inp.data_ptr(),
-                          out.data_ptr(), out.numel())
+                          out.data_ptr(), out.numel(), overlap=overlap)
         if not async_op:
             w.wait()
         return w
 
-    def all_gather(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = True):
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = True,
+                   overlap: bool = True):
         """out = every rank's inp in rank order; in place when inp is out's
         rank-th piece."""
         w = self._enqueue(_lib.lib().moonbit_nccl_all_gather_f32, inp.data_ptr(),
-                          out.data_ptr(), inp.numel())
+                          out.data_ptr(), inp.numel(), overlap=overlap)
         if not async_op:
             w.wait()
         return w
 
     # -- health and teardown
     def async_error(self) -> int:
-        return _lib.lib().moonbit_nccl_get_async_error(self.handle)
+        L = _lib.lib()
+        rc = L.moonbit_nccl_get_async_error(self.handle)
+        if rc == _lib.MX_OK and self.full_handle:
+            rc = L.moonbit_nccl_get_async_error(self.full_handle)
+        return rc
 
     def wait(self, timeout_ms: int) -> int:
         """Host watchdog over the collective stream (moonbit_nccl_wait); on
-        an error or a timeout the communicator is aborted."""
-        rc = _lib.lib().moonbit_nccl_wait(self.handle, self.stream.cuda_stream, int(timeout_ms))
+        an error or a timeout the communicators are aborted."""
+        L = _lib.lib()
+        rc = L.moonbit_nccl_wait(self.handle, self.stream.cuda_stream, int(timeout_ms))
+        if rc == _lib.MX_OK and self.full_handle:
+            rc = L.moonbit_nccl_get_async_error(self.full_handle)
         if rc != _lib.MX_OK:
-            self.handle = None
+            if self.full_handle:
+                L.moonbit_nccl_abort(self.full_handle)
+            self.handle = self.full_handle = None
         return rc
 
     def destroy(self) -> None:
-        if self.handle:
+        if self.handle or self.full_handle:
             torch.cuda.synchronize(self.device)
-            check(_lib.lib().moonbit_nccl_destroy(self.handle), "moonbit_nccl_destroy")
-            self.handle = None
+        for name in ("handle", "full_handle"):
+            h = getattr(self, name)
+            if h:
+                check(_lib.lib().moonbit_nccl_destroy(h), "moonbit_nccl_destroy")
+                setattr(self, name, None)
 
 
 class TorchCollectives:
@@ -145,16 +177,16 @@ class TorchCollectives:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
 
-    def all_reduce(self, t, async_op: bool = True):
+    def all_reduce(self, t, async_op: bool = True, overlap: bool = True):
         import torch.distributed as dist
         return dist.all_reduce(t, group=self.group, async_op=async_op) or _DoneWork()
 
-    def reduce_scatter(self, out, inp, async_op: bool = True):
+    def reduce_scatter(self, out, inp, async_op: bool = True, overlap: bool = True):
         import torch.distributed as dist
         return (dist.reduce_scatter_tensor(out, inp, group=self.group, async_op=async_op)
                 or _DoneWork())
 
-    def all_gather(self, out, inp, async_op: bool = True):
+    def all_gather(self, out, inp, async_op: bool = True, overlap: bool = True):
         import torch.distributed as dist
         return (dist.all_gather_into_tensor(out, inp, group=self.group, async_op=async_op)
                 or _DoneWork())

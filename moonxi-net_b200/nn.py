@@ -124,18 +124,21 @@ class ShardPlan:
                 out.append((a, b))
         return out
 
-    def reduce_scatter(self, buf, i, group, async_op=True):
+    def reduce_scatter(self, buf, i, group, async_op=True, overlap=True):
         """Sums bucket i of `buf` over the ranks into this rank's piece.
-        `group`: a process group (None = default) or a collectives object."""
+        `group`: a process group (None = default) or a collectives object;
+        overlap=False: nothing runs beside it (it may take every SM)."""
         s, e = self.buckets[i]
         a, b = self.pieces[i]
-        return as_collectives(group).reduce_scatter(buf[a:b], buf[s:e], async_op=async_op)
+        return as_collectives(group).reduce_scatter(buf[a:b], buf[s:e], async_op=async_op,
+                                                    overlap=overlap)
 
-    def all_gather(self, buf, i, group, async_op=True):
+    def all_gather(self, buf, i, group, async_op=True, overlap=True):
         """Fills bucket i of `buf` with every rank's piece."""
         s, e = self.buckets[i]
         a, b = self.pieces[i]
-        return as_collectives(group).all_gather(buf[s:e], buf[a:b], async_op=async_op)
+        return as_collectives(group).all_gather(buf[s:e], buf[a:b], async_op=async_op,
+                                                overlap=overlap)
 
 
 def shard_rows(global_batch: int, rank: int, world: int):
@@ -207,14 +210,17 @@ class MLP:
         # by its producer): needs TMA-legal leading dimensions (multiples of 4).
         self.fused = (precision == "3xtf32" and all(d % 4 == 0 for d in self.dims)
                       and fused is not False)
-        # Sharded update (opt-in; split-form path, several ranks): gradients
-        # are reduce-scattered instead of all-reduced, each rank updates its
-        # 1/G of the parameters, and the new weights are all-gathered layer by
-        # layer at the start of the next step, overlapping its forward, where
-        # each rank re-splits them.  Measured on 2 B200s (wide MLP) it is
-        # slower than the replicated update (1.34 vs 1.38 M samples/s: the
-        # update halves, the forward grows by the gather and the re-split),
-        # so the default stays all-reduce + replicated update.
+        # Sharded update (split-form path, several ranks): gradients are
+        # reduce-scattered instead of all-reduced, each rank updates its 1/G
+        # of the parameters, and the new weights are all-gathered layer by
+        # layer (the first at the end of the step, the others beside the next
+        # step's forward), where each rank re-splits them.  Default from 4
+        # ranks on: measured on B200s (wide MLP, global batch 8192) it gives
+        # 2.63 vs 2.40 M samples/s on 4 GPUs and 3.73 vs 3.42 M on 8, while
+        # on 2 the replicated update is ahead (1.47 vs 1.39 M: the update is
+        # only halved there, and the gathers cost the forward more).
+        if shard_update is None:
+            shard_update = self.world >= 4
         self.sharded = self.fused and self.world > 1 and bool(shard_update)
         if self.sharded:
             # the weight all-gathers run beside the forward GEMMs that need
@@ -562,10 +568,11 @@ class MLP:
                     gemm(fl, **kw)
                     if self.coll is not None and nchunk > 1:
                         works.append(self.coll.all_reduce(self.grads_buf[lo:hi]))
+            # the first layer's bucket comes last: nothing is left to overlap it
             if plan is not None:
-                works.append(plan.reduce_scatter(self.grads_buf, i, self.coll))
+                works.append(plan.reduce_scatter(self.grads_buf, i, self.coll, overlap=i > 0))
             elif self.coll is not None and nchunk == 1:
-                works.append(self.coll.all_reduce(self.bucket(i)))
+                works.append(self.coll.all_reduce(self.bucket(i), overlap=i > 0))
             if dx is not None:
                 gemm(dx[0], **dx[1])
         mark("backward")
@@ -592,7 +599,8 @@ class MLP:
         re-split them to hi/lo right behind the gather on that stream -- the
         split then runs on the SMs the GEMMs leave free, beside the forward
         of the earlier layers, instead of in front of layer i's GEMM."""
-        work = self.plan.all_gather(self._params_full, i, self.coll)
+        # the first layer's gather runs where nothing overlaps it
+        work = self.plan.all_gather(self._params_full, i, self.coll, overlap=i > 0)
         if not self._split_on_coll_stream:
             return work
         from .collectives import _EventWork
@@ -617,7 +625,7 @@ class MLP:
                 ops.sum_squares(self.grads_buf[a:b], sc[0:1], accumulate=k > 0, ctx=self.ctx)
         else:
             ops.sum_squares(self.grads_buf[:0], sc[0:1], ctx=self.ctx)
-        self.coll.all_reduce(sc).wait()
+        self.coll.all_reduce(sc, overlap=False).wait()
         if not update:
             return
         g0 = None

@@ -317,3 +317,19 @@ def test_invalid_arguments(cuda_device):
 def test_status_word_clean(cuda_device):
     rc, where = ops.status()
     assert rc == 0, (rc, where)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0)])
+def test_tf32_wide_tiles(cuda_device, ta, tb):
+    """Plain TF32 on grids of two or more waves of 256 x 256 tiles runs the
+    256-row tile (two M = 128 MMAs sharing each B tile): M and N ragged (the
+    last tile's lower 128 rows partly, and its last columns, outside the
+    output), with bias + ReLU and with alpha/beta, against fp64 at the TF32
+    tolerance; run to run bit-identical."""
+    M, K, N = 4608 + 136, 520, 4200  # 19 x 17 = 323 tiles of 256 x 256 on 148 SMs
+    C, c64, scale, _ = run_case(M, K, N, ta, tb, "tf32", seed=9, bias=True, relu=True)
+    assert rel_err(C, c64, scale) <= tol("tf32", K)
+    C2, _, _, _ = run_case(M, K, N, ta, tb, "tf32", seed=9, bias=True, relu=True)
+    assert torch.equal(C, C2)
+    C, c64, scale, _ = run_case(M, K, N, ta, tb, "tf32", seed=10, alpha=-0.5, beta=0.75)
+    assert rel_err(C, c64, scale) <= tol("tf32", K)

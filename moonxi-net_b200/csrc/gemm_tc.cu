@@ -58,17 +58,13 @@ __host__ __device__ constexpr int stage_bk() {
   return PASSES == 1 ? 32 : 16;
 }
 
-// MS: 128-row A subtiles per tile.  MS = 2 (plain TF32 only) makes a
-// 256 x 256 tile from two M = 128 MMAs that share the B tile in shared
-// memory: a third fewer operand bytes per FLOP, for the L2->SM bandwidth that
-// bounds plain TF32; both TMEM halves then hold the one tile's accumulator.
-template <int PASSES, int BK = kBK, int MS = 1>
+template <int PASSES, int BK = kBK>
 struct Cfg {
   static constexpr int kOperandCopies = PASSES == 3 ? 2 : 1;
-  static constexpr int kATileB = kBM * BK * 4;  // bytes of one 128-row subtile
+  static constexpr int kATileB = kBM * BK * 4;  // bytes
   static constexpr int kBTileB = kBN * BK * 4;
-  static constexpr int kStageBytes = kOperandCopies * (MS * kATileB + kBTileB);
-  static constexpr int kStages = MS == 2 ? 3 : (PASSES == 3 ? 4 : (BK == 32 ? 4 : 8));
+  static constexpr int kStageBytes = kOperandCopies * (kATileB + kBTileB);
+  static constexpr int kStages = PASSES == 3 ? 4 : (BK == 32 ? 4 : 8);
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
 };
 
@@ -430,19 +426,13 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int k8) {
 }
 
 // One stage of operand tiles (A hi/lo, B hi/lo) for k-blocks starting at k0.
-template <int PASSES, bool AK, bool BKM, int BK, int MS = 1>
+template <int PASSES, bool AK, bool BKM, int BK>
 __device__ __forceinline__ void load_stage(uint8_t* base, const CUtensorMap* ah,
                                            const CUtensorMap* al, const CUtensorMap* bh,
                                            const CUtensorMap* bl, uint64_t* bar, int k0, int tm,
                                            int tn, bool a3d, bool b3d) {
-  using C = Cfg<PASSES, BK, MS>;
+  using C = Cfg<PASSES, BK>;
   constexpr int kATile = C::kATileB, kBTile = C::kBTileB;
-  if (MS == 2) {  // plain TF32 256-row tile: [A rows 0-127][A rows 128-255][B]
-    load_operand<AK, kBM, BK>(base, ah, bar, k0, tm * 2 * kBM, a3d);
-    load_operand<AK, kBM, BK>(base + kATile, ah, bar, k0, tm * 2 * kBM + kBM, a3d);
-    load_operand<BKM, kBN, BK>(base + 2 * kATile, bh, bar, k0, tn * kBN, b3d);
-    return;
-  }
   load_operand<AK, kBM, BK>(base, ah, bar, k0, tm * kBM, a3d);
   if (PASSES == 3) {
     load_operand<AK, kBM, BK>(base + kATile, al, bar, k0, tm * kBM, a3d);
@@ -455,22 +445,11 @@ __device__ __forceinline__ void load_stage(uint8_t* base, const CUtensorMap* ah,
 
 // The MMAs of one stage: BK/8 slices, three TF32 MMAs per slice for 3xTF32
 // (lo_a.hi_b, hi_a.lo_b, hi_a.hi_b), one for plain TF32.
-template <int PASSES, bool AK, bool BKM, int BK, int MS = 1>
+template <int PASSES, bool AK, bool BKM, int BK>
 __device__ __forceinline__ void mma_stage(uint32_t s_base, uint32_t d_tmem, uint32_t idesc,
                                           uint32_t& accumulate) {
-  using C = Cfg<PASSES, BK, MS>;
+  using C = Cfg<PASSES, BK>;
   constexpr int kATile = C::kATileB, kBTile = C::kBTileB;
-  if (MS == 2) {  // two M = 128 MMAs per slice, sharing B; subtile s -> TMEM columns s * 256
-    const uint32_t s_b = s_base + 2 * kATile;
-#pragma unroll
-    for (int k8 = 0; k8 < BK / 8; ++k8) {
-      const uint64_t b = operand_desc<BKM, BK>(s_b, k8);
-      mma_tf32(d_tmem, operand_desc<AK, BK>(s_base, k8), b, idesc, accumulate);
-      mma_tf32(d_tmem + kBN, operand_desc<AK, BK>(s_base + kATile, k8), b, idesc, accumulate);
-      accumulate = 1u;
-    }
-    return;
-  }
   const uint32_t s_ah = s_base;
   const uint32_t s_al = s_base + kATile;
   const uint32_t s_bh = s_base + (PASSES == 3 ? 2 * kATile : kATile);
@@ -498,7 +477,7 @@ __device__ __forceinline__ void mma_stage(uint32_t s_base, uint32_t d_tmem, uint
 // typically of the other GEMM -- runs its main loop while the first tile's
 // epilogue drains, and the two GEMMs pay one launch, one prologue and one
 // unhidden epilogue between them.
-template <int PASSES, bool AK, bool BKM, bool PAIR, bool AK1, bool BK1, int MS = 1>
+template <int PASSES, bool AK, bool BKM, bool PAIR, bool AK1, bool BK1>
 __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUtensorMap* tmAl,
                                              const CUtensorMap* tmBh, const CUtensorMap* tmBl,
                                              const CUtensorMap* tmAh1, const CUtensorMap* tmAl1,
@@ -506,8 +485,7 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
                                              const TcParams& p, const TcParams& p1) {
   constexpr int BK = stage_bk<PASSES, AK, BKM>();
   static_assert(!PAIR || stage_bk<PASSES, AK1, BK1>() == BK, "paired GEMMs share the stage shape");
-  static_assert(MS == 1 || (MS == 2 && PASSES == 1 && !PAIR), "256-row tiles: plain TF32 only");
-  using C = Cfg<PASSES, BK, MS>;
+  using C = Cfg<PASSES, BK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -605,8 +583,8 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
             load_stage<PASSES, AK1, BK1, BK>(base, tmAh1, tmAl1, tmBh1, tmBl1, &full[stage], k0,
                                              tm, tn, p1.a_map3d, p1.b_map3d);
           else
-            load_stage<PASSES, AK, BKM, BK, MS>(base, tmAh, tmAl, tmBh, tmBl, &full[stage], k0,
-                                                tm, tn, p.a_map3d, p.b_map3d);
+            load_stage<PASSES, AK, BKM, BK>(base, tmAh, tmAl, tmBh, tmBl, &full[stage], k0, tm,
+                                            tn, p.a_map3d, p.b_map3d);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -632,10 +610,9 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
       int t, kb0, kb1;
       while (ok && it.next<kMma>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
         const bool q1 = second(t, kb1);
-        // two accumulators (tile i's epilogue beside tile i+1's main loop),
-        // or with 256-row tiles one that fills both TMEM halves
-        const int acc = MS == 2 ? 0 : local & 1;
-        const uint32_t acc_phase = MS == 2 ? local & 1 : (local >> 1) & 1;
+        // two accumulators: tile i's epilogue beside tile i+1's main loop
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
         ++local;
         if (!wait_bar(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, p.timeout_ns, 202)) {
           ok = false;
@@ -654,7 +631,7 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
           if (PAIR && q1)
             mma_stage<PASSES, AK1, BK1, BK>(s_base, d_tmem, idesc1, accumulate);
           else
-            mma_stage<PASSES, AK, BKM, BK, MS>(s_base, d_tmem, idesc0, accumulate);
+            mma_stage<PASSES, AK, BKM, BK>(s_base, d_tmem, idesc0, accumulate);
           tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
           if (++stage == C::kStages) {
             stage = 0;
@@ -732,8 +709,8 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
     it.init(p, num_kb);
     int t, kb0, kb1;
     while (it.next<kEpilogue>(p, num_kb, t, kb0, kb1, ring, abort_flag)) {
-      const int acc = MS == 2 ? 0 : local & 1;
-      const uint32_t acc_phase = MS == 2 ? local & 1 : (local >> 1) & 1;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
       if (!wait_bar(&acc_full[acc], acc_phase, abort_flag, p.status, p.timeout_ns, 204)) break;
       tc_fence_after();
@@ -742,13 +719,11 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
       const bool vec_ok = vec_of(q), mask_vec = mask_vec_of(q);
       int tm, tn;
       tile_coords(t, q.tiles_m, q.tiles_n, tm, tn);
-      const bool whole = MS == 2 || q1 || (kb0 == 0 && kb1 == num_kb);
+      const bool whole = q1 || (kb0 == 0 && kb1 == num_kb);
       const int rbase = lane_grp * 32;  // this warp's first row in the tile
       float* tw = &tr_buf[lane_grp][0];
-      // chunks of 32 columns; with 256-row tiles chunks 8-15 are the lower
-      // 128 rows (TMEM columns 256-511)
 #pragma unroll 1
-      for (int chunk = 0; chunk < MS * (kBN / 32); ++chunk) {
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         uint32_t r[32];
         __syncwarp();  // the previous chunk's transpose reads are done
         tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * kBN +
@@ -764,16 +739,15 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = tw[i * 33 + lane];
         if (whole) {
-          const int sub = chunk / (kBN / 32), cc = chunk % (kBN / 32);
-          const int col = tn * kBN + cc * 32 + lane;
-          store_rows(q, (tm * MS + sub) * kBM + rbase, col, v);
-          if (MS == 1 && q.colsum) {  // rows past M and columns past N hold zero
+          const int col = tn * kBN + chunk * 32 + lane;
+          store_rows(q, tm * kBM + rbase, col, v);
+          if (q.colsum) {  // rows past M and columns past N hold zero
             float cs = 0.0f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) cs += v[i];
             cs_warp[lane_grp][chunk * 32 + lane] = cs;
           }
-        } else if (MS == 1) {
+        } else {
           // partial tile: this CTA's slot, [row][256 columns]
           float* slot = p.sk_partials + own_slot(p, t, num_kb) * (kBM * kBN) +
                         static_cast<int64_t>(rbase) * kBN + chunk * 32 + lane;
@@ -783,7 +757,7 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
       }
       tc_fence_before();
       bar_arrive(&acc_empty[acc]);  // TMEM is free again; partials are in memory
-      if (MS == 1 && whole && q.colsum)
+      if (whole && q.colsum)
         colsum_commit(q, tm, tn, [&](int c) {
           return (cs_warp[0][c] + cs_warp[1][c]) + (cs_warp[2][c] + cs_warp[3][c]);
         });
@@ -888,13 +862,13 @@ __device__ __forceinline__ void tc_gemm_body(const CUtensorMap* tmAh, const CUte
   }
 }
 
-template <int PASSES, bool AK, bool BKM, int MS = 1>
+template <int PASSES, bool AK, bool BKM>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                    const TcParams p) {
-  tc_gemm_body<PASSES, AK, BKM, false, AK, BKM, MS>(&tmAh, &tmAl, &tmBh, &tmBl, &tmAh, &tmAl,
-                                                    &tmBh, &tmBl, p, p);
+  tc_gemm_body<PASSES, AK, BKM, false, AK, BKM>(&tmAh, &tmAl, &tmBh, &tmBl, &tmAh, &tmAl, &tmBh,
+                                                &tmBl, p, p);
 }
 
 // Two independent 3xTF32 GEMMs in one launch (tc_gemm_body, PAIR): p's tiles
@@ -1009,11 +983,11 @@ cudaError_t launch_split(const float* src, int64_t ld, bool kcontig, int R, int 
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-template <int PASSES, bool AK, bool BKM, int MS = 1>
+template <int PASSES, bool AK, bool BKM>
 cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                       const CUtensorMap& bl, const TcParams& p, int grid, cudaStream_t s) {
-  auto kern = tc_gemm_kernel<PASSES, AK, BKM, MS>;
-  constexpr int kSmem = Cfg<PASSES, stage_bk<PASSES, AK, BKM>(), MS>::kSmem;
+  auto kern = tc_gemm_kernel<PASSES, AK, BKM>;
+  constexpr int kSmem = Cfg<PASSES, stage_bk<PASSES, AK, BKM>()>::kSmem;
   static SmemOptIn opt_in;
   cudaError_t e = opt_in.ensure(kern, kSmem);
   if (e != cudaSuccess) return e;
@@ -1022,14 +996,14 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
   return cudaGetLastError();
 }
 
-template <int PASSES, int MS = 1>
+template <int PASSES>
 cudaError_t launch_tc_major(bool ak, bool bkm, const CUtensorMap& ah, const CUtensorMap& al,
                             const CUtensorMap& bh, const CUtensorMap& bl, const TcParams& p,
                             int grid, cudaStream_t s) {
-  if (ak && bkm) return launch_tc<PASSES, true, true, MS>(ah, al, bh, bl, p, grid, s);
-  if (ak) return launch_tc<PASSES, true, false, MS>(ah, al, bh, bl, p, grid, s);
-  if (bkm) return launch_tc<PASSES, false, true, MS>(ah, al, bh, bl, p, grid, s);
-  return launch_tc<PASSES, false, false, MS>(ah, al, bh, bl, p, grid, s);
+  if (ak && bkm) return launch_tc<PASSES, true, true>(ah, al, bh, bl, p, grid, s);
+  if (ak) return launch_tc<PASSES, true, false>(ah, al, bh, bl, p, grid, s);
+  if (bkm) return launch_tc<PASSES, false, true>(ah, al, bh, bl, p, grid, s);
+  return launch_tc<PASSES, false, false>(ah, al, bh, bl, p, grid, s);
 }
 
 // Tensor map of one split copy.  K-major: element (r, k) at base[r*ld + k],
@@ -1280,30 +1254,6 @@ int tc_gemm_split(const TcLaunch& L, const SplitOperand& A, const SplitOperand& 
   const int rc = tc_prepare(L, A, B, E, M, N, K, passes, s, maps, p);
   if (rc != kOk) return rc;
   const CUtensorMap &tah = maps[0], &tal = maps[1], &tbh = maps[2], &tbl = maps[3];
-  // Plain TF32 on a grid of at least two full waves of 256 x 256 tiles with
-  // K >= 4096 runs the 256-row tile (whole tiles; no column sums, which
-  // count 128-row tiles).  Its one accumulator leaves each tile's epilogue
-  // unhidden, which a long main loop pays for (8192^3: 699 vs 692 TFLOP/s)
-  // and a short one does not (8192 x 2048 x 8192: 450 vs 471).
-  // MX_TF32_WIDE=0 keeps 128-row tiles.
-  static const bool wide_enabled = [] {
-    const char* e = std::getenv("MX_TF32_WIDE");
-    return !(e && e[0] == '0');
-  }();
-  if (passes == 1 && wide_enabled && !E.colsum && K >= 4096) {
-    const int G = L.all_sms > L.num_sms ? L.all_sms : L.num_sms;
-    const int tiles_m2 = (M + 2 * kBM - 1) / (2 * kBM);
-    const int64_t tiles2 = static_cast<int64_t>(tiles_m2) * p.tiles_n;
-    if (tiles2 >= 2LL * G) {
-      p.tiles_m = tiles_m2;
-      p.num_tiles = static_cast<int>(tiles2);
-      const int waves2 = static_cast<int>((tiles2 + G - 1) / G);
-      const int grid2 = static_cast<int>((tiles2 + waves2 - 1) / waves2);
-      const cudaError_t e2 =
-          launch_tc_major<1, 2>(A.kmajor, B.kmajor, tah, tal, tbh, tbl, p, grid2, s);
-      return e2 == cudaSuccess ? kOk : cuda_status(e2);
-    }
-  }
   // Fewest CTAs that still finish the tiles in the same number of waves: a
   // 128- or 512-tile GEMM takes 128 SMs, leaving the rest to a concurrent
   // NCCL all-reduce at no cost to the GEMM (B200 has 148 SMs).

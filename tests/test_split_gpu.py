@@ -326,3 +326,35 @@ def test_sm_budget_is_a_preference(cuda_device):
         assert float(((c.double() - ref).abs() / scale).max()) <= 1e-5 * math.sqrt(K)
     finally:
         ops.destroy_context(ctx)
+
+
+def test_sm_limit_is_hard(cuda_device):
+    """mx_context_set_sm_limit caps the SMs whatever the cost model prefers:
+    the 512-tile GEMM that takes all 148 SMs under a 128-SM preference runs
+    four whole waves on 128 under a 128-SM limit, with the same result."""
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    M = K = N = 4096
+    g = torch.Generator("cuda").manual_seed(6)
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = torch.randn(K, N, device="cuda", generator=g)
+    ah, al = _split(A)
+    bh, bl = _split(B)
+    outs = []
+    for limit in (0, 128):
+        ctx = ops.new_context(0)
+        try:
+            ops.set_sm_budget(ctx, 128)
+            ops.set_sm_limit(ctx, limit)
+            assert ops.split_plan(M, N, K, ctx=ctx)["mode"] == (2 if limit == 0 else 0)
+            c = torch.empty(M, N, device="cuda")
+            ops.gemm_split(ah, al, K, True, bh, bl, N, False, M, K, N, c=c, padded=3, ctx=ctx)
+            torch.cuda.synchronize()
+            assert ops.context_status(ctx)[0] == 0
+            outs.append(c)
+        finally:
+            ops.destroy_context(ctx)
+    ref = A.double() @ B.double()
+    scale = A.double().abs() @ B.double().abs()
+    for c in outs:
+        assert float(((c.double() - ref).abs() / scale).max()) <= 1e-5 * math.sqrt(K)
